@@ -1,0 +1,171 @@
+"""torch-tensor front end of the native attention library.
+
+Mirrors the reference's Python entry points (base/baseline_gqa.py:57-59
+``sdpa_gqa(q, k, v, scale)``, base/baseline_gqa_causal.py:61-65
+``sdpa_gqa_causal``) and its CUDA launchers' argument meaning
+(B, Hq, Hkv, S, G, scale; BHSD layout; hkv = hq // G).  Tensors are [B, H, S, D]
+views; any view whose last dimension is contiguous works (a BSHD tensor
+``x.transpose(1, 2)`` is passed through its strides, no copy).  Everything runs
+in the native library on the current CUDA stream; there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _ffi
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _bhs(t: torch.Tensor):
+    if t.dim() != 4 or t.stride(3) != 1:
+        raise ValueError("expected a [B, H, S, D] tensor with a contiguous last dimension")
+    return (t.stride(0), t.stride(1), t.stride(2))
+
+
+def _check_inputs(q, k, v):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+    B, Hq, Sq, D = q.shape
+    Bk, Hkv, Skv, Dk = k.shape
+    if v.shape != k.shape or Bk != B or Dk != D:
+        raise ValueError(f"shape mismatch q={tuple(q.shape)} k={tuple(k.shape)} v={tuple(v.shape)}")
+    if Hq % Hkv:
+        raise ValueError("Hq must be a multiple of Hkv")
+    return B, Hq, Hkv, Sq, Skv, D
+
+
+def _strides(q, k, v, o):
+    s = _ffi.BwStrides()
+    for field, t in (("q", q), ("k", k), ("v", v), ("o", o)):
+        getattr(s, field)[:] = _bhs(t)
+    return ctypes.byref(s)
+
+
+def _attn(q, k, v, scale, causal, out=None, lse=None, return_lse=True):
+    B, Hq, Hkv, Sq, Skv, D = _check_inputs(q, k, v)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o = out if out is not None else torch.empty((B, Hq, Sq, D), dtype=torch.bfloat16, device=q.device)
+    if return_lse and lse is None:
+        lse = torch.empty((B, Hq, Sq), dtype=torch.float32, device=q.device)
+    G = Hq // Hkv
+    rc = _ffi.lib().bw_gqa_split_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, Hq, Hkv, Sq, Skv, G, D,
+                                     float(scale), int(bool(causal)), _strides(q, k, v, o), _stream())
+    _ffi.check(rc, "bw_gqa_split_fwd")
+    return o, lse
+
+
+def gqa_fwd(q, k, v, scale=None, out=None, lse=None):
+    """Non-causal GQA forward -> (O bf16 [B,Hq,S,D], LSE fp32 [B,Hq,S])."""
+    if q.shape[2] != k.shape[2]:
+        raise ValueError("gqa_fwd needs Sq == Skv (use gqa_split_fwd)")
+    return _attn(q, k, v, scale, False, out, lse)
+
+
+def gqa_causal_fwd(q, k, v, scale=None, out=None, lse=None):
+    """Causal GQA forward (key j visible to query i iff j <= i) -> (O, LSE)."""
+    if q.shape[2] != k.shape[2]:
+        raise ValueError("gqa_causal_fwd needs Sq == Skv")
+    return _attn(q, k, v, scale, True, out, lse)
+
+
+def gqa_split_fwd(q, k, v, scale=None, causal=False, out=None, lse=None):
+    """GQA forward with Sq != Skv (the reference's split-length launcher) -> (O, LSE)."""
+    return _attn(q, k, v, scale, causal, out, lse)
+
+
+def mha_fwd(q, k, v, scale=None, out=None, lse=None):
+    """MHA forward (Hq == Hkv) -> (O, LSE)."""
+    if q.shape[1] != k.shape[1]:
+        raise ValueError("mha_fwd needs equal head counts")
+    return _attn(q, k, v, scale, False, out, lse)
+
+
+def sdpa_gqa(q, k, v, scale):
+    """Drop-in for base/baseline_gqa.py:57-59: returns O only."""
+    return _attn(q, k, v, scale, False, return_lse=False)[0]
+
+
+def sdpa_gqa_causal(q, k, v, scale):
+    """Drop-in for base/baseline_gqa_causal.py:61-65: returns O only."""
+    return _attn(q, k, v, scale, True, return_lse=False)[0]
+
+
+def decode_workspace_size(B, Hq, Hkv, D, total_tokens, chunk=0):
+    return int(_ffi.lib().bw_gqa_decode_workspace_size(B, Hq, Hkv, D, int(total_tokens), int(chunk)))
+
+
+def gqa_decode(q, k, v, kv_lens, kv_offsets, scale=None, chunk=0, workspace=None, out=None, lse=None):
+    """Single-token split-KV GQA decode over ragged contiguous KV.
+
+    q [B, Hq, D] bf16; k, v [total_tokens, Hkv, D] bf16; kv_lens int32 [B];
+    kv_offsets int64 [B] (first token of each sequence).  Returns (O [B,Hq,D] bf16,
+    LSE [B,Hq] fp32)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+    if kv_lens.dtype != torch.int32 or kv_offsets.dtype != torch.int64:
+        raise TypeError("kv_lens must be int32 and kv_offsets int64")
+    B, Hq, D = q.shape
+    total, Hkv, Dk = k.shape
+    if Dk != D or v.shape != k.shape or kv_lens.numel() != B or kv_offsets.numel() != B:
+        raise ValueError("shape mismatch")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    need = decode_workspace_size(B, Hq, Hkv, D, total, chunk)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    o = out if out is not None else torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    rc = _ffi.lib().bw_gqa_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(kv_lens), _ptr(kv_offsets), _ptr(o), _ptr(lse),
+                                  B, Hq, Hkv, D, int(total), float(scale), int(chunk), _ptr(workspace),
+                                  workspace.numel() * workspace.element_size(), _stream())
+    _ffi.check(rc, "bw_gqa_decode")
+    return o, lse
+
+
+def lse_combine(o_part, lse_part, out=None, lse=None):
+    """Merge split partials: o_part fp32 [S, B, Hq, D], lse_part fp32 [S, B, Hq]."""
+    S, B, Hq, D = o_part.shape
+    if lse_part.shape != (S, B, Hq) or o_part.dtype != torch.float32 or lse_part.dtype != torch.float32:
+        raise ValueError("bad partial shapes / dtypes")
+    o_part, lse_part = o_part.contiguous(), lse_part.contiguous()
+    o = out if out is not None else torch.empty((B, Hq, D), dtype=torch.bfloat16, device=o_part.device)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=o_part.device)
+    rc = _ffi.lib().bw_lse_combine(_ptr(o_part), _ptr(lse_part), S, B, Hq, D, _ptr(o), _ptr(lse), _stream())
+    _ffi.check(rc, "bw_lse_combine")
+    return o, lse
+
+
+def stream_status() -> int:
+    """Synchronise the current stream and return (and clear) the device error code."""
+    return int(_ffi.lib().bw_stream_status(_stream()))
+
+
+def set_option(key: int, value: int) -> None:
+    _ffi.check(_ffi.lib().bw_set_option(key, int(value)), "bw_set_option")
+
+
+def get_option(key: int) -> int:
+    return int(_ffi.lib().bw_get_option(key))
+
+
+def shard_plan(units: int, world: int, rank: int):
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    _ffi.check(_ffi.lib().bw_shard_plan(units, world, rank, ctypes.byref(b), ctypes.byref(e)), "bw_shard_plan")
+    return b.value, e.value

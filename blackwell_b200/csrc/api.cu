@@ -1,0 +1,361 @@
+// C-ABI entry points (include/bw_attn.h): argument validation, TMA tensor-map
+// encoding, per-device state, and dispatch to the kernels.
+#include <atomic>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "../../include/bw_attn.h"
+#include "kernels.h"
+
+namespace {
+
+// Device error word: 0, or 0x100|site for a timed-out wait, 0x200 for a decode
+// workspace overflow.  One per device (module globals are per context).
+__device__ int g_bw_err;
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool init = false;
+  int num_sms = 0;
+  int* err = nullptr;
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+std::atomic<int64_t> g_timeout_ns{2000000000LL};
+std::atomic<int64_t> g_p_in_tmem{1};
+std::atomic<int64_t> g_debug_flags{0};
+std::atomic<int64_t> g_max_ctas{0};
+
+int get_device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BW_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    if (cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return BW_ERR_CUDA;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_bw_err) != cudaSuccess) return BW_ERR_CUDA;
+    st.err = static_cast<int*>(p);
+    if (!g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || !fn)
+        return BW_ERR_CUDA;
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    st.init = true;
+  }
+  *out = &st;
+  return BW_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 4-D map over a [B, H, S, D] bf16 tensor with element strides (sb, sh, ss, 1):
+// dims (D, S, H, B), box (64, 128, 1, 1), 128-byte swizzle, zero fill out of bounds.
+int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, const int64_t st[3]) {
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
+}
+
+// 2-D map over [rows, cols] bf16 (row stride = cols), box (64, 64), 128B swizzle.
+int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
+}
+
+bool strides_ok(const int64_t s[3]) {
+  for (int i = 0; i < 3; ++i)
+    if (s[i] <= 0 || (s[i] % 8) != 0 || s[i] * 2 >= (int64_t(1) << 40)) return false;
+  return true;
+}
+
+void contiguous(int H, int S, int D, int64_t out[3]) {
+  out[2] = D;
+  out[1] = (int64_t)S * D;
+  out[0] = (int64_t)H * S * D;
+}
+
+int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int Sq,
+             int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream) {
+  if (!Q || !K || !V || !O) return BW_ERR_NULL;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0 || G <= 0) return BW_ERR_SHAPE;
+  if (Hq % Hkv != 0 || Hq / Hkv != G) return BW_ERR_SHAPE;
+  if (D != 64 && D != 128) return BW_ERR_SHAPE;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return BW_ERR_SHAPE;
+  if ((int64_t)B * Hq * ((Sq + 255) / 256) >= (int64_t(1) << 30)) return BW_ERR_SHAPE;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return BW_ERR_ALIGN;
+  bw_strides st;
+  if (strides) {
+    st = *strides;
+  } else {
+    contiguous(Hq, Sq, D, st.q);
+    contiguous(Hkv, Skv, D, st.k);
+    contiguous(Hkv, Skv, D, st.v);
+    contiguous(Hq, Sq, D, st.o);
+  }
+  if (!strides_ok(st.q) || !strides_ok(st.k) || !strides_ok(st.v) || !strides_ok(st.o)) return BW_ERR_ALIGN;
+
+  DeviceState* dev = nullptr;
+  int rc = get_device_state(&dev);
+  if (rc != BW_OK) return rc;
+
+  bw::FmhaMaps maps;
+  if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_bhsd(&maps.k, K, B, Hkv, Skv, D, st.k) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_bhsd(&maps.v, V, B, Hkv, Skv, D, st.v) != BW_OK) return BW_ERR_CUDA;
+
+  bw::FmhaParams p{};
+  p.O = O;
+  p.o_sb = st.o[0];
+  p.o_sh = st.o[1];
+  p.o_ss = st.o[2];
+  p.LSE = LSE;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = G;
+  p.Sq = Sq;
+  p.Skv = Skv;
+  p.D = D;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.n_qtiles = (Sq + 127) / 128;
+  p.n_kvtiles = (Skv + 127) / 128;
+  p.pair_heads = (G % 2 == 0) ? 1 : 0;
+  p.num_items = p.pair_heads ? B * (Hq / 2) * p.n_qtiles : B * Hq * ((p.n_qtiles + 1) / 2);
+  p.err = dev->err;
+  p.timeout_ns = (uint64_t)g_timeout_ns.load();
+  p.debug_flags = (int)g_debug_flags.load();
+  int ctas = dev->num_sms;
+  const int64_t cap = g_max_ctas.load();
+  if (cap > 0 && cap < ctas) ctas = (int)cap;
+  cudaError_t e = bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, ctas, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
+}
+
+constexpr int kDefaultChunk = 1024;
+
+int64_t decode_max_parts(int B, int Hkv, int64_t total_tokens, int chunk) {
+  return (int64_t)Hkv * ((total_tokens + chunk - 1) / chunk + B);
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" {
+
+int bw_gqa_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int S,
+               int G, int D, float scale, const bw_strides* strides, void* stream) {
+  return attn_fwd(Q, K, V, O, LSE, B, Hq, Hkv, S, S, G, D, scale, 0, strides, stream);
+}
+
+int bw_gqa_causal_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv,
+                      int S, int G, int D, float scale, const bw_strides* strides, void* stream) {
+  return attn_fwd(Q, K, V, O, LSE, B, Hq, Hkv, S, S, G, D, scale, 1, strides, stream);
+}
+
+int bw_gqa_split_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv,
+                     int Sq, int Skv, int G, int D, float scale, int causal, const bw_strides* strides,
+                     void* stream) {
+  return attn_fwd(Q, K, V, O, LSE, B, Hq, Hkv, Sq, Skv, G, D, scale, causal, strides, stream);
+}
+
+int bw_mha_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int H, int S, int D,
+               float scale, const bw_strides* strides, void* stream) {
+  return attn_fwd(Q, K, V, O, LSE, B, H, H, S, S, 1, D, scale, 0, strides, stream);
+}
+
+size_t bw_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int64_t total_tokens, int chunk) {
+  if (B <= 0 || Hkv <= 0 || Hq % Hkv != 0 || total_tokens < 0) return 0;
+  if (chunk <= 0) chunk = kDefaultChunk;
+  const int G = Hq / Hkv;
+  const int64_t parts = decode_max_parts(B, Hkv, total_tokens, chunk);
+  return align256((size_t)(B + 1) * 4) + align256((size_t)parts * G * 4) + (size_t)parts * G * D * 4;
+}
+
+int bw_gqa_decode(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets,
+                  void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (!Q || !K || !V || !kv_lens || !kv_offsets || !O || !workspace) return BW_ERR_NULL;
+  if (B <= 0 || B > 4096 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0) return BW_ERR_SHAPE;
+  const int G = Hq / Hkv;
+  if (G > 16 || (D != 64 && D != 128) || total_tokens <= 0 || total_tokens >= (int64_t(1) << 31))
+    return BW_ERR_SHAPE;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return BW_ERR_SHAPE;
+  if (chunk <= 0) chunk = kDefaultChunk;
+  if (chunk % 64 != 0) return BW_ERR_SHAPE;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(workspace))
+    return BW_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(kv_offsets) & 7u) || (reinterpret_cast<uintptr_t>(kv_lens) & 3u))
+    return BW_ERR_ALIGN;
+  if (workspace_bytes < bw_gqa_decode_workspace_size(B, Hq, Hkv, D, total_tokens, chunk)) return BW_ERR_WORKSPACE;
+
+  DeviceState* dev = nullptr;
+  int rc = get_device_state(&dev);
+  if (rc != BW_OK) return rc;
+
+  bw::DecodeMaps maps;
+  if (make_map_2d(&maps.k, K, total_tokens, (int64_t)Hkv * D) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_2d(&maps.v, V, total_tokens, (int64_t)Hkv * D) != BW_OK) return BW_ERR_CUDA;
+
+  const int64_t parts = decode_max_parts(B, Hkv, total_tokens, chunk);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* prefix = reinterpret_cast<int*>(ws);
+  float* lse_part = reinterpret_cast<float*>(ws + align256((size_t)(B + 1) * 4));
+  float* o_part = reinterpret_cast<float*>(ws + align256((size_t)(B + 1) * 4) + align256((size_t)parts * G * 4));
+
+  bw::DecodeParams p{};
+  p.Q = Q;
+  p.q_sb = (int64_t)Hq * D;
+  p.q_sh = D;
+  p.kv_lens = kv_lens;
+  p.kv_offsets = kv_offsets;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = G;
+  p.D = D;
+  p.chunk = chunk;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o_part = o_part;
+  p.lse_part = lse_part;
+  p.chunk_prefix = prefix;
+  p.max_parts = (int)parts;
+  p.err = dev->err;
+  p.timeout_ns = (uint64_t)g_timeout_ns.load();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = bw::launch_decode(p, maps, dev->num_sms, s);
+  if (e != cudaSuccess) return BW_ERR_CUDA;
+
+  bw::CombineParams c{};
+  c.o_part = o_part;
+  c.lse_part = lse_part;
+  c.chunk_prefix = prefix;
+  c.splits = 0;
+  c.B = B;
+  c.Hq = Hq;
+  c.Hkv = Hkv;
+  c.G = G;
+  c.D = D;
+  c.O = O;
+  c.o_sb = (int64_t)Hq * D;
+  c.o_sh = D;
+  c.LSE = LSE;
+  e = bw::launch_lse_combine(c, s);
+  return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
+}
+
+int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
+                   float* LSE, void* stream) {
+  if (!O_part || !LSE_part || !O) return BW_ERR_NULL;
+  if (splits <= 0 || B <= 0 || Hq <= 0 || D <= 0 || D % 4 != 0 || D > 128) return BW_ERR_SHAPE;
+  if (!aligned16(O_part) || (reinterpret_cast<uintptr_t>(O) & 7u)) return BW_ERR_ALIGN;
+  bw::CombineParams c{};
+  c.o_part = O_part;
+  c.lse_part = LSE_part;
+  c.chunk_prefix = nullptr;
+  c.splits = splits;
+  c.B = B;
+  c.Hq = Hq;
+  c.Hkv = Hq;
+  c.G = 1;
+  c.D = D;
+  c.O = O;
+  c.o_sb = (int64_t)Hq * D;
+  c.o_sh = D;
+  c.LSE = LSE;
+  cudaError_t e = bw::launch_lse_combine(c, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
+}
+
+int bw_stream_status(void* stream) {
+  DeviceState* dev = nullptr;
+  int rc = get_device_state(&dev);
+  if (rc != BW_OK) return rc;
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return BW_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, dev->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return BW_ERR_CUDA;
+  if (v != 0) {
+    const int zero = 0;
+    if (cudaMemcpy(dev->err, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return BW_ERR_CUDA;
+  }
+  if (v == 0) return BW_OK;
+  if (v & 0x200) return BW_ERR_WORKSPACE;
+  return BW_ERR_TIMEOUT;
+}
+
+int bw_set_option(int key, int64_t value) {
+  switch (key) {
+    case BW_OPT_TIMEOUT_NS:
+      if (value <= 0) return BW_ERR_SHAPE;
+      g_timeout_ns = value;
+      return BW_OK;
+    case BW_OPT_P_IN_TMEM: g_p_in_tmem = value ? 1 : 0; return BW_OK;
+    case BW_OPT_DEBUG_FLAGS: g_debug_flags = value; return BW_OK;
+    case BW_OPT_MAX_CTAS:
+      if (value < 0) return BW_ERR_SHAPE;
+      g_max_ctas = value;
+      return BW_OK;
+    default: return BW_ERR_SHAPE;
+  }
+}
+
+int64_t bw_get_option(int key) {
+  switch (key) {
+    case BW_OPT_TIMEOUT_NS: return g_timeout_ns.load();
+    case BW_OPT_P_IN_TMEM: return g_p_in_tmem.load();
+    case BW_OPT_DEBUG_FLAGS: return g_debug_flags.load();
+    case BW_OPT_MAX_CTAS: return g_max_ctas.load();
+    default: return -1;
+  }
+}
+
+int bw_shard_plan(int64_t units, int world, int rank, int64_t* begin, int64_t* end) {
+  if (!begin || !end) return BW_ERR_NULL;
+  if (units < 0 || world <= 0 || rank < 0 || rank >= world) return BW_ERR_SHAPE;
+  const int64_t base = units / world, rem = units % world;
+  *begin = rank * base + (rank < rem ? rank : rem);
+  *end = *begin + base + (rank < rem ? 1 : 0);
+  return BW_OK;
+}
+
+const char* bw_strerror(int code) {
+  switch (code) {
+    case BW_OK: return "ok";
+    case BW_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case BW_ERR_ALIGN: return "pointer or stride not 16-byte aligned";
+    case BW_ERR_CUDA: return "CUDA call failed";
+    case BW_ERR_TIMEOUT: return "device-side wait timed out";
+    case BW_ERR_NCCL: return "collective failed";
+    case BW_ERR_NULL: return "required pointer is NULL";
+    case BW_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown error";
+  }
+}
+
+const char* bw_version(void) { return "bw_attn 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

@@ -1,0 +1,70 @@
+// Internal launch interface between the C-ABI layer (api.cu) and the kernels.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace bw {
+
+// Prefill / full-sequence attention forward (GQA, MHA = GQA with G = 1).
+struct FmhaParams {
+  void* O;                       // bf16, element strides below (d stride 1)
+  int64_t o_sb, o_sh, o_ss;
+  float* LSE;                    // fp32 [B, Hq, Sq] contiguous, may be null
+  int B, Hq, Hkv, G, Sq, Skv, D;
+  int causal;                    // 1: key j visible to query i iff j <= i
+  float scale_log2;              // softmax scale * log2(e)
+  int n_qtiles, n_kvtiles;       // ceil(Sq / 128), ceil(Skv / 128)
+  int pair_heads;                // 1: a CTA work item = two heads of one KV group,
+                                 //    same 128-row query tile; 0: two query tiles of one head
+  int num_items;
+  int* err;                      // device error word
+  uint64_t timeout_ns;           // bound for every device-side wait
+  int debug_flags;               // bit 0: producer withholds its first K load (timeout test)
+};
+
+struct FmhaMaps {
+  CUtensorMap q, k, v;           // 4-D (D, S, H, B) bf16, box (64, 128, 1, 1), SWIZZLE_128B
+};
+
+cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int num_sms,
+                            cudaStream_t stream);
+
+// Split-KV single-token decode over ragged, contiguous per-sequence KV.
+struct DecodeParams {
+  const void* Q;                 // bf16 [B, Hq, D], strides q_sb, q_sh
+  int64_t q_sb, q_sh;
+  const int* kv_lens;            // [B]
+  const int64_t* kv_offsets;     // [B] first token of sequence b
+  int B, Hq, Hkv, G, D;
+  int chunk;                     // tokens per split (multiple of 64)
+  float scale_log2;
+  float* o_part;                 // [parts, G, D] fp32, normalised by its own sum
+  float* lse_part;               // [parts, G]   natural-log LSE of the split
+  int* chunk_prefix;             // [B + 1] written by the decode kernel
+  int max_parts;                 // capacity of o_part / lse_part (bounds check)
+  int* err;
+  uint64_t timeout_ns;
+};
+
+struct DecodeMaps {
+  CUtensorMap k, v;              // 2-D (Hkv*D, total_tokens) bf16, box (64, 64), SWIZZLE_128B
+};
+
+cudaError_t launch_decode(const DecodeParams& p, const DecodeMaps& maps, int num_sms, cudaStream_t stream);
+
+// Merge of split partials.
+struct CombineParams {
+  const float* o_part;           // ragged: [parts, G, D] via chunk_prefix; uniform: [splits, B, Hq, D]
+  const float* lse_part;         // ragged: [parts, G];                     uniform: [splits, B, Hq]
+  const int* chunk_prefix;       // null => uniform `splits`
+  int splits;
+  int B, Hq, Hkv, G, D;
+  void* O;                       // bf16 [B, Hq, D] (strides o_sb, o_sh)
+  int64_t o_sb, o_sh;
+  float* LSE;                    // fp32 [B, Hq], may be null
+};
+
+cudaError_t launch_lse_combine(const CombineParams& p, cudaStream_t stream);
+
+}  // namespace bw

@@ -1,0 +1,138 @@
+/* bw_attn.h -- C ABI of the B200 (sm_100a) GQA / MHA attention forward.
+ *
+ * Drop-in boundary for the attention path of the reference workbench
+ * (sanjaykrishnablubridge-bit/Blackwell).  Each entry point names the reference
+ * launcher it replaces.  Conventions, shared by every call:
+ *
+ *  - Tensors are caller-owned DEVICE buffers on the current CUDA device.  The
+ *    library allocates nothing; the decode path takes a caller workspace.
+ *  - Q, K, V, O are bf16 (raw 16-bit storage, `const void*`).  LSE is fp32,
+ *    natural log, [B, Hq, Sq] contiguous (may be NULL: not written).
+ *  - Default layout is the reference's BHSD, contiguous: [B, H, S, D].  Any other
+ *    layout whose head dimension is contiguous (e.g. BSHD) is passed with
+ *    `bw_strides` (element strides of the b, h, s axes).  Strides must be
+ *    multiples of 8 elements (16 bytes); base pointers 16-byte aligned.
+ *  - GQA routing: query head hq reads KV head hq / G, G = Hq / Hkv.
+ *  - D (head dimension) is 64 or 128.  The reference fixes it as a template
+ *    parameter (`template<int Br,int Bc,int D>`); here it is a runtime argument.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *    asynchronous; they are reentrant and may be made from several host threads.
+ *  - Return codes (never exit()): BW_OK, or an error below.  Argument errors are
+ *    detected before any launch.  Device-side failures (a bounded wait that
+ *    timed out, a workspace that was too small for the actual lengths) are
+ *    recorded in a per-device error word that bw_stream_status() reads.
+ */
+#ifndef BW_ATTN_H_
+#define BW_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BW_API __attribute__((visibility("default")))
+#else
+#define BW_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  BW_OK = 0,
+  BW_ERR_SHAPE = 1,     /* unsupported or inconsistent sizes */
+  BW_ERR_ALIGN = 2,     /* pointer or stride not 16-byte aligned */
+  BW_ERR_CUDA = 3,      /* a CUDA runtime / driver call failed */
+  BW_ERR_TIMEOUT = 4,   /* a device-side wait exceeded its bound */
+  BW_ERR_NCCL = 5,      /* collective failure (multi-GPU helpers) */
+  BW_ERR_NULL = 6,      /* required pointer is NULL */
+  BW_ERR_WORKSPACE = 7  /* workspace too small */
+};
+
+/* Element strides of the batch, head and sequence axes (head-dim stride is 1). */
+typedef struct bw_strides {
+  int64_t q[3];
+  int64_t k[3];
+  int64_t v[3];
+  int64_t o[3];
+} bw_strides;
+
+/* Non-causal GQA forward, Sq = Skv = S.
+ * Replaces launch_gqa_v0..v23<Br,Bc,D>(Q,K,V,O,LSE,B,Hq,Hkv,S,G,scale)
+ * (src/SM103/attention/GQA_sm103.cu:5733-6516; the sm_120 twins in
+ * src/SM120/attention/GQA_sm120.cu:353-380). */
+BW_API int bw_gqa_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int S,
+               int G, int D, float scale, const bw_strides* strides, void* stream);
+
+/* Causal GQA forward (key j visible to query i iff j <= i).
+ * Replaces launch_gqa_vN_causal<Br,Bc,D>(Q,K,V,O,LSE,B,Hq,Hkv,S,G,scale)
+ * (src/SM103/attention/GQA_sm103_causal.cu:4155-7760,
+ *  src/SM103/attention/GQA_sm103_causal_v3.cu:2156-2180). */
+BW_API int bw_gqa_causal_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv,
+                      int S, int G, int D, float scale, const bw_strides* strides, void* stream);
+
+/* Split-length GQA forward, Sq != Skv (cross-attention / KV-cache prefill).
+ * Replaces launch_gqa_v1<Br,Bc,D>(Q,K,V,O,LSE,B,Hq,Hkv,Sq,Skv,G,scale)
+ * (src/SM120/attention/adhitya_GQA.cu:199-213).  `causal` = 0 matches the
+ * reference; 1 applies the top-left mask j <= i. */
+BW_API int bw_gqa_split_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv,
+                     int Sq, int Skv, int G, int D, float scale, int causal, const bw_strides* strides,
+                     void* stream);
+
+/* MHA forward (G = 1), bf16 in/out, optional LSE.
+ * Replaces mha_v3_tc<Br,Bc,D><<<(S/Br,B*H),32,smem>>>(Q,K,V,O,scale,S)
+ * (src/SM120/attention/MHA_sm120.cu:64-71, launch :333-345), which is fp32
+ * in/out without LSE. */
+BW_API int bw_mha_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int H, int S, int D,
+               float scale, const bw_strides* strides, void* stream);
+
+/* Split-KV single-token decode.  No counterpart kernel exists in the reference;
+ * the semantics are its split-length GQA (adhitya_GQA.cu:63-188) with Sq = 1
+ * and Skv = kv_lens[b] per sequence.
+ *   Q:  bf16 [B, Hq, D] contiguous
+ *   K, V: bf16 [total_tokens, Hkv, D] contiguous; sequence b owns tokens
+ *         [kv_offsets[b], kv_offsets[b] + kv_lens[b])   (device int64 / int32)
+ *   O:  bf16 [B, Hq, D];  LSE: fp32 [B, Hq] or NULL
+ * `chunk` = tokens per split (multiple of 64; 0 = default 1024).  The KV of one
+ * sequence is split into ceil(L_b / chunk) pieces whose partials are merged by
+ * the LSE-combine kernel on the same stream.  `workspace` must hold
+ * bw_gqa_decode_workspace_size(B, Hq, Hkv, D, total_tokens, chunk) bytes. */
+BW_API size_t bw_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int64_t total_tokens, int chunk);
+BW_API int bw_gqa_decode(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets,
+                  void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge `splits` partial attention results (new; no reference counterpart).
+ *   O_part fp32 [splits, B, Hq, D], each normalised by its own softmax sum;
+ *   LSE_part fp32 [splits, B, Hq] (natural log; -inf = empty split).
+ * Writes O bf16 [B, Hq, D] and LSE fp32 [B, Hq] (may be NULL). */
+BW_API int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
+                   float* LSE, void* stream);
+
+/* Synchronise `stream`, then read and clear this device's error word.
+ * Returns BW_OK, BW_ERR_TIMEOUT, BW_ERR_WORKSPACE or BW_ERR_CUDA. */
+BW_API int bw_stream_status(void* stream);
+
+/* Library options (process-wide).  Keys:
+ *   BW_OPT_TIMEOUT_NS      bound on every device-side wait (default 2e9)
+ *   BW_OPT_P_IN_TMEM       1 (default): P feeds the PV MMA from tensor memory;
+ *                          0: through a swizzled shared-memory tile
+ *   BW_OPT_DEBUG_FLAGS     test hook; bit 0 makes the prefill producer withhold
+ *                          its first K tile so that the consumers' bounded waits
+ *                          expire and the call reports BW_ERR_TIMEOUT
+ *   BW_OPT_MAX_CTAS        cap on the persistent prefill grid (0 = SM count) */
+enum { BW_OPT_TIMEOUT_NS = 1, BW_OPT_P_IN_TMEM = 2, BW_OPT_DEBUG_FLAGS = 3, BW_OPT_MAX_CTAS = 4 };
+BW_API int bw_set_option(int key, int64_t value);
+BW_API int64_t bw_get_option(int key);
+
+/* Contiguous share [*begin, *end) of `units` work units for `rank` of `world`
+ * (multi-GPU sharding by (batch x KV-head group); no collective). */
+BW_API int bw_shard_plan(int64_t units, int world, int rank, int64_t* begin, int64_t* end);
+
+BW_API const char* bw_strerror(int code);
+BW_API const char* bw_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BW_ATTN_H_ */

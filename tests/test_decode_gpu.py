@@ -1,0 +1,71 @@
+"""Split-KV decode and LSE-combine parity (through the C ABI)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as orc
+from tests._util import LSE_TOL, O_TOL, bf16_from_bits, seeded_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _decode(q, k, v, lens, chunk=0):
+    import blackwell_b200 as bw
+    lens = np.asarray(lens)
+    offs = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    o, lse = bw.gqa_decode(q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(lens.astype(np.int32)).cuda(),
+                           torch.from_numpy(offs).cuda(), chunk=chunk)
+    assert bw.stream_status() == 0
+    return o.float().cpu().numpy(), lse.cpu().numpy(), offs
+
+
+@pytest.mark.parametrize("chunk", [0, 64, 256])
+def test_decode_golden(golden, chunk):
+    g = golden("decode_d128")
+    q, k, v = (bf16_from_bits(g[n]) for n in ("q_bf16", "k_bf16", "v_bf16"))
+    o, lse, _ = _decode(q, k, v, g["kv_lens"], chunk)
+    assert np.abs(o - g["o_fp64"]).max() <= O_TOL
+    assert np.abs(lse - g["lse_fp64"]).max() <= LSE_TOL
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,maxlen,chunk", [
+    (5, 64, 8, 128, 3000, 1024), (3, 8, 8, 64, 700, 128), (4, 16, 1, 128, 2100, 512), (2, 12, 4, 64, 200, 64)])
+def test_decode_ragged(B, Hq, Hkv, D, maxlen, chunk):
+    rng = np.random.default_rng(B * 1000 + D)
+    lens = rng.integers(1, maxlen + 1, B)
+    lens[0] = 1
+    total = int(lens.sum())
+    q = seeded_bf16((B, Hq, D), 11)
+    k = seeded_bf16((total, Hkv, D), 12)
+    v = seeded_bf16((total, Hkv, D), 13)
+    o, lse, offs = _decode(q, k, v, lens, chunk)
+    ro, rl = orc.decode_reference(q.float(), k.float(), v.float(), lens, offs, 1 / math.sqrt(D))
+    assert np.abs(o - ro).max() <= O_TOL
+    assert np.abs(lse - rl).max() <= LSE_TOL
+
+
+def test_decode_empty_sequence_gives_zero():
+    q = seeded_bf16((2, 8, 128), 1)
+    k = seeded_bf16((100, 1, 128), 2)
+    v = seeded_bf16((100, 1, 128), 3)
+    o, lse, _ = _decode(q, k, v, [0, 100])
+    assert np.all(o[0] == 0) and np.all(np.isneginf(lse[0]))
+    ro, rl = orc.decode_reference(q[1:].float(), k.float(), v.float(), [100], [0], 1 / math.sqrt(128))
+    assert np.abs(o[1] - ro[0]).max() <= O_TOL
+
+
+@pytest.mark.parametrize("splits", [1, 3, 64])
+def test_lse_combine_kernel(splits):
+    import blackwell_b200 as bw
+    rng = np.random.default_rng(splits)
+    B, Hq, D = 3, 5, 128
+    op = rng.standard_normal((splits, B, Hq, D)).astype(np.float32)
+    lp = (rng.standard_normal((splits, B, Hq)) * 3).astype(np.float32)
+    if splits > 1:
+        lp[0, 0, 0] = -np.inf
+    o, lse = bw.lse_combine(torch.from_numpy(op).cuda(), torch.from_numpy(lp).cuda())
+    ro, rl = orc.lse_combine_reference(op, lp)
+    assert np.abs(o.float().cpu().numpy() - ro).max() <= O_TOL
+    assert np.abs(lse.cpu().numpy() - rl).max() <= 1e-5

@@ -1,0 +1,34 @@
+"""Failure detection without a GPU fault: every device-side wait is bounded.
+A test hook makes the producer withhold its first K tile; the consumers' waits
+expire after the (short) configured bound, the kernel unwinds, and the call
+reports BW_ERR_TIMEOUT.  The context stays usable for the next call."""
+import math
+
+import pytest
+import torch
+
+from tests._util import seeded_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def test_withheld_tile_reports_timeout_and_recovers():
+    import blackwell_b200 as bw
+    from blackwell_b200 import _ffi
+    q = seeded_bf16((1, 2, 256, 64), 1).cuda()
+    k = seeded_bf16((1, 2, 256, 64), 2).cuda()
+    v = seeded_bf16((1, 2, 256, 64), 3).cuda()
+    old_t = bw.get_option(_ffi.BW_OPT_TIMEOUT_NS)
+    try:
+        bw.set_option(_ffi.BW_OPT_TIMEOUT_NS, 50_000_000)   # 50 ms
+        bw.set_option(_ffi.BW_OPT_DEBUG_FLAGS, 1)
+        bw.mha_fwd(q, k, v)
+        assert bw.stream_status() == _ffi.BW_ERR_TIMEOUT
+    finally:
+        bw.set_option(_ffi.BW_OPT_DEBUG_FLAGS, 0)
+        bw.set_option(_ffi.BW_OPT_TIMEOUT_NS, old_t)
+    assert bw.stream_status() == 0
+    o, lse = bw.mha_fwd(q, k, v)
+    assert bw.stream_status() == 0
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float())
+    assert (o.float() - ref).abs().max().item() < 2e-2

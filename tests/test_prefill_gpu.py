@@ -1,0 +1,133 @@
+"""Parity of the sm_100a attention forward (through the C ABI) with the oracle.
+
+Bar: max-abs error <= 2e-2 on bf16 O and <= 1e-3 on LSE against the fp64
+restatement of the reference's ground truth, on the same bf16 input bits."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as orc
+from tests._util import LSE_TOL, O_TOL, bf16_from_bits, seeded_bf16
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN_GQA = ["gqa_nc_d128", "gqa_causal_d128", "gqa_causal_d64_g3_rand", "gqa_causal_d64_ragged", "gqa_split_d64"]
+
+
+@pytest.fixture(scope="module", params=[1, 0], ids=["p_tmem", "p_smem"])
+def p_variant(request):
+    import blackwell_b200 as bw
+    from blackwell_b200 import _ffi
+    old = bw.get_option(_ffi.BW_OPT_P_IN_TMEM)
+    bw.set_option(_ffi.BW_OPT_P_IN_TMEM, request.param)
+    yield request.param
+    bw.set_option(_ffi.BW_OPT_P_IN_TMEM, old)
+
+
+def _run(q, k, v, scale, causal):
+    import blackwell_b200 as bw
+    o, lse = bw.gqa_split_fwd(q.cuda(), k.cuda(), v.cuda(), scale, causal=causal)
+    assert bw.stream_status() == 0
+    return o.float().cpu().numpy(), lse.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", GOLDEN_GQA)
+def test_golden(golden, name, p_variant):
+    g = golden(name)
+    q, k, v = (bf16_from_bits(g[n]) for n in ("q_bf16", "k_bf16", "v_bf16"))
+    o, lse = _run(q, k, v, float(g["scale"]), bool(g["causal"]))
+    assert np.abs(o - g["o_fp64"]).max() <= O_TOL
+    assert np.abs(lse - g["lse_fp64"]).max() <= LSE_TOL
+
+
+def test_c1_shape_in_bf16(golden, p_variant):
+    """C1's shape (B=1,Hq=8,Hkv=2,S=512,D=64) on the GPU, inputs rounded to bf16."""
+    g = golden("c1_gqa_fp32")
+    q, k, v = (torch.from_numpy(g[n]).bfloat16() for n in ("q_f32", "k_f32", "v_f32"))
+    o, lse = _run(q, k, v, float(g["scale"]), False)
+    ro, rl = orc.fp64_reference(q.float(), k.float(), v.float(), float(g["scale"]))
+    assert np.abs(o - ro).max() <= O_TOL
+    assert np.abs(lse - rl).max() <= LSE_TOL
+
+
+CASES = [
+    # B, Hq, Hkv, Sq, Skv, D, causal
+    (1, 2, 2, 1, 1, 64, False),
+    (1, 2, 1, 1, 1, 128, True),
+    (2, 4, 4, 77, 77, 64, True),      # MHA, ragged S
+    (1, 8, 1, 128, 128, 128, True),    # G = 8
+    (1, 3, 1, 300, 300, 128, False),   # G = 3 (odd: query-tile pairs)
+    (2, 4, 2, 513, 513, 128, True),
+    (1, 6, 2, 257, 640, 64, False),    # split lengths
+    (1, 4, 2, 640, 200, 128, True),    # Sq > Skv, causal
+    (1, 2, 1, 1, 1000, 128, False),    # one query row
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c)))
+def test_shapes(case, p_variant):
+    B, Hq, Hkv, Sq, Skv, D, causal = case
+    q = seeded_bf16((B, Hq, Sq, D), 1)
+    k = seeded_bf16((B, Hkv, Skv, D), 2)
+    v = seeded_bf16((B, Hkv, Skv, D), 3)
+    scale = 1 / math.sqrt(D)
+    o, lse = _run(q, k, v, scale, causal)
+    ro, rl = orc.fp64_reference(q.float(), k.float(), v.float(), scale, causal=causal)
+    assert np.abs(o - ro).max() <= O_TOL
+    assert np.abs(lse - rl).max() <= LSE_TOL
+
+
+def test_bshd_layout_strides():
+    """BSHD storage passed through strides (the C2 layout), no copies."""
+    import blackwell_b200 as bw
+    B, S, Hq, Hkv, D = 2, 384, 8, 2, 128
+    qs = seeded_bf16((B, S, Hq, D), 4)
+    ks = seeded_bf16((B, S, Hkv, D), 5)
+    vs = seeded_bf16((B, S, Hkv, D), 6)
+    out = torch.empty((B, S, Hq, D), dtype=torch.bfloat16, device="cuda")
+    o, lse = bw.gqa_causal_fwd(qs.cuda().transpose(1, 2), ks.cuda().transpose(1, 2), vs.cuda().transpose(1, 2),
+                               1 / math.sqrt(D), out=out.transpose(1, 2))
+    assert bw.stream_status() == 0
+    ro, rl = orc.fp64_reference(qs.transpose(1, 2).float(), ks.transpose(1, 2).float(), vs.transpose(1, 2).float(),
+                                1 / math.sqrt(D), causal=True)
+    assert np.abs(out.transpose(1, 2).float().cpu().numpy() - ro).max() <= O_TOL
+    assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL
+
+
+def test_c2_full_size_rows():
+    """C2 at full size (B=4,Hq=32,Hkv=8,S=4096,D=128, causal, BSHD): 2048 random
+    rows against the fp64 row oracle, plus size-independent properties."""
+    import blackwell_b200 as bw
+    B, S, Hq, Hkv, D = 4, 4096, 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(42)
+    q = torch.randn(B, S, Hq, D, generator=g, device="cuda").bfloat16()
+    k = torch.randn(B, S, Hkv, D, generator=g, device="cuda").bfloat16()
+    v = torch.randn(B, S, Hkv, D, generator=g, device="cuda").bfloat16()
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    o, lse = bw.gqa_causal_fwd(qt, kt, vt, 1 / math.sqrt(D))
+    assert bw.stream_status() == 0
+    assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
+    rng = np.random.default_rng(7)
+    rows = np.stack([rng.integers(0, B, 2048), rng.integers(0, Hq, 2048), rng.integers(0, S, 2048)], 1)
+    rows[:8, 2] = [0, 1, 127, 128, 4095, 4094, 2047, 2048]
+    qc, kc, vc = qt.float().cpu(), kt.float().cpu(), vt.float().cpu()
+    ro, rl = orc.fp64_rows(qc, kc, vc, 1 / math.sqrt(D), True, rows)
+    oc, lc = o.float().cpu().numpy(), lse.cpu().numpy()
+    got_o = np.stack([oc[b, h, i] for b, h, i in rows])
+    got_l = np.array([lc[b, h, i] for b, h, i in rows])
+    assert np.abs(got_o - ro).max() <= O_TOL
+    assert np.abs(got_l - rl).max() <= LSE_TOL
+    # row 0 sees only key 0: O = V[0]
+    assert torch.allclose(o[:, :, 0].float(), vt[:, :, 0].repeat_interleave(Hq // Hkv, 1).float(), atol=1e-2)
+
+
+def test_deterministic_and_out_of_place():
+    import blackwell_b200 as bw
+    q = seeded_bf16((1, 4, 700, 128), 8).cuda()
+    k = seeded_bf16((1, 2, 700, 128), 9).cuda()
+    v = seeded_bf16((1, 2, 700, 128), 10).cuda()
+    o1, l1 = bw.gqa_causal_fwd(q, k, v)
+    o2, l2 = bw.gqa_causal_fwd(q, k, v)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
