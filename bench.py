@@ -1,0 +1,403 @@
+"""Benchmark of the B200 attention forward (headline: causal GQA prefill, C2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload ("C2"): causal GQA prefill,
+B=4, Hq=32, Hkv=8 (G=4), S=4096, D=128, BSHD layout, bf16 in / fp32 accumulate,
+Q/K/V ~ N(0,1) from seed 42 (synthetic; no dataset).  A step is one forward
+over that batch.  Metric: TFLOP/s with the FA/SDPA causal count
+4*B*Hq*S^2*D/2 = 5.498e11 FLOP per step.
+
+Timing: W untimed warm-up steps, then K timed steps between a barrier +
+synchronize on both sides.  Before every step a 256 MiB buffer is written to
+flush L2; each step is bracketed by CUDA events on the launching stream (the
+flush is outside the event pair).  ``value`` = FLOPs of all ranks / max over
+ranks of the summed step times.  ``e2e`` repeats the step through the public
+API with pinned host buffers: H2D of Q, K, V, the forward, D2H of O and LSE.
+
+Multi-GPU (torchrun, one rank per GPU, NCCL): the work shards by
+(batch x KV-head group) with no collective on the data path; every rank runs
+its own B=4 shard (weak scaling, global batch 4N).
+
+``--impl reference`` times the reference's own CPU path for this workload
+(torch SDPA with enable_gqa, base/baseline_gqa_causal.py:61-65, restated in
+oracle/attention_oracle.py:sdpa_cpu) on the host cores, one bounded sample
+per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+C2 = dict(B=4, Hq=32, Hkv=8, S=4096, D=128)
+METRIC = "GQA fwd TFLOP/s/GPU & % BF16 tensor peak; split-KV decode HBM GB/s & % peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def causal_flops(B, Hq, S, D):
+    return 4.0 * B * Hq * S * S * D / 2
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM traffic recorded from an ncu capture in profiles/<name>."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        mhz, maxmhz, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm, mx, pw = float(r[0]), float(r[1]), float(r[2])
+            except (ValueError, IndexError):
+                continue
+            maxmhz = mx
+            if pw > 200:  # under load
+                mhz.append(sm)
+            for n, v in zip(names, r[4:8]):
+                if "Active" in v and "Not" not in v:
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": maxmhz,
+                "reasons": sorted(reasons), "samples_under_load": len(mhz)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU path
+class CpuReference:
+    """The reference's CPU path (torch SDPA, enable_gqa, causal) on one (b, KV-group)
+    slice of C2: G=4 query heads x S=4096 x D=128, bf16, all host cores."""
+
+    def __init__(self):
+        from oracle.attention_oracle import sdpa_cpu
+        self.fn = sdpa_cpu
+        self.cores = os.cpu_count() or 1
+        torch.set_num_threads(self.cores)
+        G, S, D = C2["Hq"] // C2["Hkv"], C2["S"], C2["D"]
+        g = torch.Generator().manual_seed(42)
+        self.q = torch.randn(1, G, S, D, generator=g).bfloat16()
+        self.k = torch.randn(1, 1, S, D, generator=g).bfloat16()
+        self.v = torch.randn(1, 1, S, D, generator=g).bfloat16()
+        self.scale = 1 / math.sqrt(D)
+        self.flops = causal_flops(1, G, S, D)
+        self.sample = f"1 (b, KV-group) slice of C2 = {G} heads x S={S} x D={D} bf16 causal per step"
+
+    def step(self):
+        """Seconds for one sample."""
+        t0 = time.perf_counter()
+        self.fn(self.q, self.k, self.v, self.scale, causal=True)
+        return time.perf_counter() - t0
+
+    def measure(self, budget_s=10.0, max_reps=200):
+        self.step()
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while not times or (time.perf_counter() < t_end and len(times) < max_reps):
+            times.append(self.step())
+        t = statistics.median(times)
+        return {"value": self.flops / t / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                "kind": "port", "sample": self.sample + f", median of {len(times)}"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    ref = CpuReference()
+    for _ in range(args.warmup):
+        ref.step()
+    t = [ref.step() for _ in range(args.steps)]
+    value = ref.flops * len(t) / sum(t) / 1e12
+    cpu = {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+           "sample": ref.sample}
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(t) / len(t),
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1), seed 42", "scaling": "weak",
+            "config": {"workload": "C2 causal GQA prefill B=4 Hq=32 Hkv=8 S=4096 D=128 BSHD",
+                       "cpu_sample": ref.sample},
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "vs_baseline": None}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU path
+def c2_inputs(rank, device):
+    B, Hq, Hkv, S, D = (C2[k] for k in ("B", "Hq", "Hkv", "S", "D"))
+    g = torch.Generator(device=device).manual_seed(42 + rank)
+    q = torch.randn(B, S, Hq, D, generator=g, device=device).bfloat16()
+    k = torch.randn(B, S, Hkv, D, generator=g, device=device).bfloat16()
+    v = torch.randn(B, S, Hkv, D, generator=g, device=device).bfloat16()
+    return q, k, v
+
+
+def time_steps(fn, steps, warmup, flush, world):
+    """Per-step CUDA-event times (ms) of `fn` on the current stream, L2 flushed before each."""
+    for _ in range(warmup):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        flush()
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def bench_decode(flush, steps, warmup):
+    """C4: split-KV decode B=64, Hq=64, Hkv=8, D=128, L_b ~ U[1024, 32768] (seed 42)."""
+    import blackwell_b200 as bw
+    B, Hq, Hkv, D = 64, 64, 8, 128
+    lens = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(42))
+    total = int(lens.sum())
+    offs = torch.cumsum(lens, 0) - lens
+    g = torch.Generator(device="cuda").manual_seed(42)
+    q = torch.randn(B, Hq, D, generator=g, device="cuda").bfloat16()
+    k = torch.randn(total, Hkv, D, generator=g, device="cuda").bfloat16()
+    v = torch.randn(total, Hkv, D, generator=g, device="cuda").bfloat16()
+    lens_d, offs_d = lens.int().cuda(), offs.long().cuda()
+    ws = torch.empty(bw.attention.decode_workspace_size(B, Hq, Hkv, D, total), dtype=torch.uint8, device="cuda")
+    o = torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, Hq, dtype=torch.float32, device="cuda")
+    fn = lambda: bw.gqa_decode(q, k, v, lens_d, offs_d, workspace=ws, out=o, lse=lse)
+    ms = time_steps(fn, steps, warmup, flush, 1)
+    assert bw.stream_status() == 0
+    nbytes = 2 * total * Hkv * D * 2 + 2 * B * Hq * D * 2 + B * Hq * 4
+    t = statistics.median(ms)
+    del k, v
+    return {"workload": "C4 split-KV decode B=64 Hq=64 Hkv=8 D=128 L~U[1024,32768] seed 42 (+LSE-combine)",
+            "sum_L": total, "ms": t, "GB/s": nbytes / t / 1e6, "algorithmic_bytes": nbytes, "launches_per_step": 2}
+
+
+def bench_prefill(shape, causal, layout, flush, steps, warmup):
+    import blackwell_b200 as bw
+    B, Hq, Hkv, S, D = shape
+    g = torch.Generator(device="cuda").manual_seed(42)
+    if layout == "bshd":
+        q = torch.randn(B, S, Hq, D, generator=g, device="cuda").bfloat16().transpose(1, 2)
+        k = torch.randn(B, S, Hkv, D, generator=g, device="cuda").bfloat16().transpose(1, 2)
+        v = torch.randn(B, S, Hkv, D, generator=g, device="cuda").bfloat16().transpose(1, 2)
+    else:
+        q = torch.randn(B, Hq, S, D, generator=g, device="cuda").bfloat16()
+        k = torch.randn(B, Hkv, S, D, generator=g, device="cuda").bfloat16()
+        v = torch.randn(B, Hkv, S, D, generator=g, device="cuda").bfloat16()
+    o = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, Hq, S, dtype=torch.float32, device="cuda")
+    fn = lambda: bw.gqa_split_fwd(q, k, v, 1 / math.sqrt(D), causal=causal, out=o, lse=lse)
+    ms = time_steps(fn, steps, warmup, flush, 1)
+    assert bw.stream_status() == 0
+    flops = causal_flops(B, Hq, S, D) if causal else 4.0 * B * Hq * S * S * D
+    t = statistics.median(ms)
+    return {"ms": t, "TFLOP/s": flops / t / 1e9}
+
+
+def run_ours(args, world, rank, local):
+    import blackwell_b200 as bw
+    from blackwell_b200 import _ffi
+    _ffi.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks, peak_kind = load_peaks()
+    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.zero_()
+
+    B, Hq, Hkv, S, D = (C2[k] for k in ("B", "Hq", "Hkv", "S", "D"))
+    q, k, v = c2_inputs(rank, dev)
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    o = torch.empty(B, S, Hq, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, Hq, S, dtype=torch.float32, device=dev)
+    scale = 1 / math.sqrt(D)
+    step = lambda: bw.gqa_causal_fwd(qt, kt, vt, scale, out=o.transpose(1, 2), lse=lse)
+
+    with ClockSampler(local) as clk:
+        ms = time_steps(step, args.steps, args.warmup, flush, world)
+    rc = bw.stream_status()
+    if rc != 0:
+        raise RuntimeError(f"device error {rc}")
+    total_ms = sum(ms)
+    total_ms_max = max_over_ranks(total_ms, world)
+    flops = causal_flops(B, Hq, S, D)
+    value = flops * args.steps * world / (total_ms_max * 1e-3) / 1e12
+    per_launch_ms = total_ms / args.steps
+    achieved = flops / (per_launch_ms * 1e-3) / 1e12
+
+    # ---- end to end through the public API with pinned host buffers
+    e2e_steps = 3 if args.profile else max(3, min(args.steps, 20))
+    hq_, hk_, hv_ = (x.cpu().pin_memory() for x in (q, k, v))
+    ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+    hl = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq_, non_blocking=True)
+        dk.copy_(hk_, non_blocking=True)
+        dv.copy_(hv_, non_blocking=True)
+        bw.gqa_causal_fwd(dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2), scale, out=o.transpose(1, 2),
+                          lse=lse)
+        ho.copy_(o, non_blocking=True)
+        hl.copy_(lse, non_blocking=True)
+
+    ms_e2e = time_steps(e2e_step, e2e_steps, 2, lambda: None, world)
+    e2e_ms_max = max_over_ranks(sum(ms_e2e), world)
+    e2e_value = flops * e2e_steps * world / (e2e_ms_max * 1e-3) / 1e12
+    h2d = sum(x.numel() * x.element_size() for x in (hq_, hk_, hv_))
+    d2h = ho.numel() * ho.element_size() + hl.numel() * hl.element_size()
+
+    secondary = {}
+    if rank == 0 and world == 1 and not (args.no_secondary or args.profile):
+        del hq_, hk_, hv_, dq, dk, dv
+        torch.cuda.empty_cache()
+        sec_steps = max(5, min(args.steps // 10, 50))
+        secondary["C3_mha_D64"] = bench_prefill((8, 16, 16, 2048, 64), False, "bhsd", flush, sec_steps, 3)
+        secondary["C3_mha_D128"] = bench_prefill((8, 16, 16, 2048, 128), False, "bhsd", flush, sec_steps, 3)
+        ref_shape = bench_prefill((8, 12, 4, 4096, 64), True, "bhsd", flush, sec_steps, 3)
+        ref_shape["reference_V46_B300_ms"] = 0.5863
+        secondary["reference_shape_causal_B8_Hq12_Hkv4_S4096_D64"] = ref_shape
+        for key in ("C3_mha_D64", "C3_mha_D128", "reference_shape_causal_B8_Hq12_Hkv4_S4096_D64"):
+            secondary[key]["frac_of_peak"] = secondary[key]["TFLOP/s"] / peaks["bf16_tflops"]
+        dec = bench_decode(flush, sec_steps, 3)
+        dec["frac_of_hbm_peak"] = dec["GB/s"] / peaks["hbm_gbs"]
+        secondary["C4_decode"] = dec
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.profile:
+        cpu = CpuReference().measure(budget_s=10.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_launch_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seed 42 (+rank)",
+            "config": {"workload": "C2 causal GQA prefill (Llama-3-8B attention shape)", "model": "gqa_causal_fwd",
+                       "global_batch": B * world, "seq_len": S, "heads_q": Hq, "heads_kv": Hkv, "head_dim": D,
+                       "layout": "BSHD", "parallelism": f"shard by batch x KV-group, {world} rank(s), no collective",
+                       "l2": "256 MiB buffer written before every step, outside the event pair",
+                       "flops_per_step": flops, "flop_count": "4*B*Hq*S^2*D/2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_tflops"], "peak_kind": f"{peak_kind} bf16 burst",
+                         "traffic": profile_traffic("fmha_fwd_c2_launches.md")},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="short run for profiler captures: no secondary configs, no CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
