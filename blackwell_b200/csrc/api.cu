@@ -165,6 +165,18 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace
 
+namespace bw {
+int device_context(int** err, int* num_sms, void** encode_fn) {
+  DeviceState* dev = nullptr;
+  const int rc = get_device_state(&dev);
+  if (rc != BW_OK) return rc;
+  *err = dev->err;
+  *num_sms = dev->num_sms;
+  *encode_fn = reinterpret_cast<void*>(g_encode);
+  return BW_OK;
+}
+}  // namespace bw
+
 extern "C" {
 
 int bw_gqa_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int S,

@@ -67,4 +67,8 @@ struct CombineParams {
 
 cudaError_t launch_lse_combine(const CombineParams& p, cudaStream_t stream);
 
+// Per-device state owned by api.cu: the device error word, the SM count and the
+// driver's cuTensorMapEncodeTiled.  Returns a bw_attn status code.
+int device_context(int** err, int* num_sms, void** encode_fn);
+
 }  // namespace bw

@@ -102,6 +102,22 @@ BW_API int bw_gqa_decode(const void* Q, const void* K, const void* V, const int*
                   void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same decode for callers that cannot allocate device memory (no
+ * counterpart in the reference: it is an addition of this library).  Callers
+ * such as allocator hooks, memory-pool callbacks or host runtimes that own no
+ * allocator cannot supply bw_gqa_decode's workspace; this variant takes none
+ * and allocates nothing.  Its scratch is a fixed array of
+ * bw_gqa_decode_static_scratch_bytes() (32 MiB) in the library's device data,
+ * held on every GPU that loads the library until exit; calls needing more
+ * (bw_gqa_decode_workspace_size with the same arguments) fail with
+ * BW_ERR_WORKSPACE.  All calls on a device share the array, so calls that
+ * overlap on the GPU race.  The first call on a device does a one-time set-up
+ * (symbol-address lookup); make it before any stream capture. */
+BW_API size_t bw_gqa_decode_static_scratch_bytes(void);
+BW_API int bw_gqa_decode_static(const void* Q, const void* K, const void* V, const int* kv_lens,
+                                const int64_t* kv_offsets, void* O, float* LSE, int B, int Hq, int Hkv, int D,
+                                int64_t total_tokens, float scale, int chunk, void* stream);
+
 /* Merge `splits` partial attention results (new; no reference counterpart).
  *   O_part fp32 [splits, B, Hq, D], each normalised by its own softmax sum;
  *   LSE_part fp32 [splits, B, Hq] (natural log; -inf = empty split).
