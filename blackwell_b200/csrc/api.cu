@@ -33,6 +33,7 @@ std::atomic<int64_t> g_timeout_ns{2000000000LL};
 std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
+std::atomic<int64_t> g_exp_poly{2};
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -151,7 +152,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   int ctas = dev->num_sms;
   const int64_t cap = g_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = (int)cap;
-  cudaError_t e = bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, ctas, static_cast<cudaStream_t>(stream));
+  cudaError_t e = bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
@@ -331,6 +332,10 @@ int bw_set_option(int key, int64_t value) {
       if (value < 0) return BW_ERR_SHAPE;
       g_max_ctas = value;
       return BW_OK;
+    case BW_OPT_EXP_POLY:
+      if (value != 0 && value != 2 && value != 3 && value != 4) return BW_ERR_SHAPE;
+      g_exp_poly = value;
+      return BW_OK;
     default: return BW_ERR_SHAPE;
   }
 }
@@ -341,6 +346,7 @@ int64_t bw_get_option(int key) {
     case BW_OPT_P_IN_TMEM: return g_p_in_tmem.load();
     case BW_OPT_DEBUG_FLAGS: return g_debug_flags.load();
     case BW_OPT_MAX_CTAS: return g_max_ctas.load();
+    case BW_OPT_EXP_POLY: return g_exp_poly.load();
     default: return -1;
   }
 }

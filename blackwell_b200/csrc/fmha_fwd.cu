@@ -30,6 +30,7 @@
 // for whichever m was used.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "softmax_math.cuh"
 #include "tmem_io.cuh"
 
 namespace bw {
@@ -264,12 +265,6 @@ __device__ void mma_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const W
   drain_wait(&bars.mma_done, 0, wc.timeout_ns);
 }
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -277,7 +272,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 // ----------------------------------------------------------- softmax warpgroups
 // Thread t of warpgroup w owns query row t of block w (TMEM lane t).
-template <int D, bool PT>
+template <int D, bool PT, int POLY>
 __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const WaitCtl& wc, uint32_t tmem,
                              int w, int t) {
   using L = Layout<D, PT>;
@@ -311,29 +306,60 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
         for (int i = 0; i < 128; ++i)
           if (i >= lim) s[i] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max: eight independent three-input max chains.
+      float mx;
+      {
+        float a[8];
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+        for (int u = 0; u < 8; ++u) a[u] = fmaxf(s[u], s[8 + u]);
+#pragma unroll
+        for (int i = 16; i < 128; i += 16)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
+        mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+      }
       const float m_cand = mx * c;
       float corr = 1.f;
       const bool upd = m_cand > m_run + 8.f;
       if (upd) {
-        corr = ex2(m_run - m_cand);
+        corr = ex2_mufu(m_run - m_cand);
         m_run = m_cand;
       }
       const float msub = (m_run == -INFINITY) ? 0.f : m_run;
-      float sum0 = 0.f, sum1 = 0.f;
+      const f2 cc2{c, c}, nm2{-msub, -msub};
+      // Phase 1: exponent arguments in place (independent paired FMAs).
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        s[i] = ex2(fmaf(s[i], c, -msub));
-        s[i + 1] = ex2(fmaf(s[i + 1], c, -msub));
-        sum0 += s[i];
-        sum1 += s[i + 1];
+      for (int k = 0; k < 64; ++k) {
+        const f2 x = ffma2(f2{s[2 * k], s[2 * k + 1]}, cc2, nm2);
+        s[2 * k] = x.x;
+        s[2 * k + 1] = x.y;
       }
-      l_run = l_run * corr + (sum0 + sum1);
+      // Phase 2: exponentials in place; POLY of every 8 pairs on the FMA pipe.
+#pragma unroll
+      for (int k = 0; k < 64; ++k) {
+        if ((k & 7) < POLY) {
+          const f2 e = ex2_poly2(f2{s[2 * k], s[2 * k + 1]});
+          s[2 * k] = e.x;
+          s[2 * k + 1] = e.y;
+        } else {
+          s[2 * k] = ex2_mufu(s[2 * k]);
+          s[2 * k + 1] = ex2_mufu(s[2 * k + 1]);
+        }
+      }
+      // Phase 3: row sum (four paired accumulators) and bf16 packing.
+      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 64; k += 4) {
+        acc0 = fadd2(acc0, f2{s[2 * k], s[2 * k + 1]});
+        acc1 = fadd2(acc1, f2{s[2 * k + 2], s[2 * k + 3]});
+        acc2 = fadd2(acc2, f2{s[2 * k + 4], s[2 * k + 5]});
+        acc3 = fadd2(acc3, f2{s[2 * k + 6], s[2 * k + 7]});
+      }
       uint32_t pk[64];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) pk[i] = pack_bf16(s[2 * i], s[2 * i + 1]);
+      for (int k = 0; k < 64; ++k) pk[k] = pack_bf16(s[2 * k], s[2 * k + 1]);
+      acc0 = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
+      l_run = l_run * corr + (acc0.x + acc0.y);
       if constexpr (PT) {
         tmem_st32(s_tmem, pk);
         tmem_st32(s_tmem + 32, pk + 32);
@@ -387,7 +413,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
   }
 }
 
-template <int D, bool PT>
+template <int D, bool PT, int POLY>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
   using L = Layout<D, PT>;
@@ -427,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, warp};
 
   if (warp < 8) {
-    softmax_role<D, PT>(p, smem, bars, wc, tmem, warp >> 2, tid & 127);
+    softmax_role<D, PT, POLY>(p, smem, bars, wc, tmem, warp >> 2, tid & 127);
   } else if (warp == 8) {
     if (lane == 0) producer_role<D, PT>(p, maps, smem, bars, wc);
   } else {
@@ -441,10 +467,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D, bool PT>
+template <int D, bool PT, int POLY>
 cudaError_t launch_impl(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
   constexpr int bytes = Layout<D, PT>::kBytes + 1024;
-  auto kern = fmha_fwd_kernel<D, PT>;
+  auto kern = fmha_fwd_kernel<D, PT, POLY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
   const int grid = p.num_items < num_sms ? p.num_items : num_sms;
@@ -452,14 +478,25 @@ cudaError_t launch_impl(const FmhaParams& p, const FmhaMaps& maps, int num_sms, 
   return cudaGetLastError();
 }
 
+template <int D, bool PT>
+cudaError_t launch_poly(const FmhaParams& p, const FmhaMaps& maps, int poly, int num_sms, cudaStream_t stream) {
+  switch (poly) {
+    case 0: return launch_impl<D, PT, 0>(p, maps, num_sms, stream);
+    case 2: return launch_impl<D, PT, 2>(p, maps, num_sms, stream);
+    case 3: return launch_impl<D, PT, 3>(p, maps, num_sms, stream);
+    case 4: return launch_impl<D, PT, 4>(p, maps, num_sms, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace
 
-cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int num_sms,
+cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int exp_poly, int num_sms,
                             cudaStream_t stream) {
-  if (p.D == 128) return p_in_tmem ? launch_impl<128, true>(p, maps, num_sms, stream)
-                                   : launch_impl<128, false>(p, maps, num_sms, stream);
-  if (p.D == 64) return p_in_tmem ? launch_impl<64, true>(p, maps, num_sms, stream)
-                                  : launch_impl<64, false>(p, maps, num_sms, stream);
+  if (p.D == 128) return p_in_tmem ? launch_poly<128, true>(p, maps, exp_poly, num_sms, stream)
+                                   : launch_poly<128, false>(p, maps, exp_poly, num_sms, stream);
+  if (p.D == 64) return p_in_tmem ? launch_poly<64, true>(p, maps, exp_poly, num_sms, stream)
+                                  : launch_poly<64, false>(p, maps, exp_poly, num_sms, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -27,7 +27,9 @@ struct FmhaMaps {
   CUtensorMap q, k, v;           // 4-D (D, S, H, B) bf16, box (64, 128, 1, 1), SWIZZLE_128B
 };
 
-cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int num_sms,
+// exp_poly: of every 8 pairs of exponentials, how many run as the FMA-pipe
+// polynomial instead of MUFU ex2 (0, 2, 3 or 4).
+cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int exp_poly, int num_sms,
                             cudaStream_t stream);
 
 // Split-KV single-token decode over ragged, contiguous per-sequence KV.
