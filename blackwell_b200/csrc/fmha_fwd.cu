@@ -36,7 +36,6 @@
 namespace bw {
 namespace {
 
-constexpr int kThreads = 320;
 constexpr int kRows = 128;          // query rows per block == KV rows per tile
 constexpr int kSmemBudget = 232448 - 2048;
 
@@ -142,7 +141,9 @@ __device__ void producer_role(const FmhaParams& p, const FmhaMaps& maps, uint8_t
       for (int kind = 0; kind < 2; ++kind) {
         const uint32_t slot = ld % NS;
         const uint32_t ph = (ld / NS) & 1;
+        BW_TRACE_AT(true, 23, ld);
         if (!wc.wait(&bars.kv_empty[slot], ph ^ 1)) { ok = false; break; }
+        BW_TRACE_AT(true, 24, ld);
         const bool withhold = kind == 0 && first_k && (p.debug_flags & 1);
         if (kind == 0) first_k = false;
         if (!withhold) {
@@ -191,27 +192,35 @@ __device__ void mma_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const W
   bool ok = true;
 
   auto kv_wait = [&](uint32_t i) -> bool { return wc.wait(&bars.kv_full[i % NS], (i / NS) & 1); };
+  // Descriptor low halves of the tile bases, computed once; each K-step adds
+  // its byte offset / 16.
+  constexpr uint32_t HI = sdesc_hi_sbo1024();
+  const uint32_t q_lo0 = sdesc_lo(smem_base + L::kQ, 16);
+  const uint32_t kv_lo_k0 = sdesc_lo(smem_base + L::kKV, 16);       // K operand (K-major)
+  const uint32_t kv_lo_v0 = sdesc_lo(smem_base + L::kKV, SUB);      // V operand (MN-major)
+  const uint32_t p_lo0 = sdesc_lo(smem_base + L::kP, 16);
   auto issue_qk = [&](int w, uint32_t kslot) {
-    const uint32_t qa = smem_base + L::kQ + w * TB;
-    const uint32_t ka = smem_base + L::kKV + kslot * TB;
+    const uint32_t qa = q_lo0 + (uint32_t)(w * TB) / 16;
+    const uint32_t ka = kv_lo_k0 + kslot * (uint32_t)(TB / 16);
     const uint32_t d_tmem = tmem + w * 128;
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
-      const uint32_t off = (ks >> 2) * SUB + (ks & 3) * 32;
-      mma_ss(d_tmem, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), IDESC_QK, ks > 0);
+      const uint32_t off = ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
+      mma_ss_lh(d_tmem, qa + off, HI, ka + off, HI, IDESC_QK, ks > 0);
     }
   };
   auto issue_pv = [&](int w, uint32_t vslot, bool acc) {
-    const uint32_t va = smem_base + L::kKV + vslot * TB;
+    const uint32_t va = kv_lo_v0 + vslot * (uint32_t)(TB / 16);
     const uint32_t o_tmem = tmem + 256 + w * D;
+    const uint32_t acc0 = acc ? 1u : 0u;
 #pragma unroll
     for (int ks = 0; ks < kRows / 16; ++ks) {
-      const uint64_t bdesc = sdesc_sw128(va + ks * 16 * 128, SUB, 1024);
+      const uint32_t b_lo = va + (ks * 16 * 128) / 16;
       if constexpr (PT) {
-        mma_ts(o_tmem, tmem + w * 128 + ks * 8, bdesc, IDESC_PV, (acc || ks > 0) ? 1u : 0u);
+        mma_ts_lh(o_tmem, tmem + w * 128 + ks * 8, b_lo, HI, IDESC_PV, ks > 0 ? 1u : acc0);
       } else {
-        const uint32_t pa = smem_base + L::kP + w * Cfg<D>::kPBytes + (ks >> 2) * SUB + (ks & 3) * 32;
-        mma_ss(o_tmem, sdesc_sw128(pa, 16, 1024), bdesc, IDESC_PV, (acc || ks > 0) ? 1u : 0u);
+        const uint32_t pa = p_lo0 + (uint32_t)(w * Cfg<D>::kPBytes) / 16 + ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
+        mma_ss_lh(o_tmem, pa, HI, b_lo, HI, IDESC_PV, ks > 0 ? 1u : acc0);
       }
     }
   };
@@ -237,19 +246,25 @@ __device__ void mma_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const W
       const uint32_t iv = ld + 2 * j + 1;
       const uint32_t ik = ld + 2 * j + 2;
       const bool next = j + 1 < it.nmax;
+      BW_TRACE_AT(true, 20, pc[0]);
       if (!kv_wait(iv)) { ok = false; break; }
+      BW_TRACE_AT(true, 21, pc[0]);
       if (next && !kv_wait(ik)) { ok = false; break; }
+      BW_TRACE_AT(true, 22, pc[0]);
       for (int w = 0; w < 2; ++w) {
         if (j < it.nkv[w]) {
           if (!wc.wait(&bars.p_full[w], pc[w] & 1)) { ok = false; break; }
           ++pc[w];
           tc_fence_after();
+          BW_TRACE_AT(true, 50 + w, pc[w] - 1);
           issue_pv(w, iv % NS, j > 0);
+          BW_TRACE_AT(true, 55 + w, pc[w] - 1);
           if (j == it.nkv[w] - 1) tc_commit(&bars.o_full[w]);
         }
         if (j + 1 < it.nkv[w]) {
           issue_qk(w, ik % NS);
           tc_commit(&bars.s_full[w]);
+          BW_TRACE_AT(true, 60 + w, pc[w] - 1);
           if (j + 2 == it.nkv[w]) tc_commit(&bars.q_empty[w]);
         }
       }
@@ -294,6 +309,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
       if (!wc.wait(&bars.s_full[w], sc & 1)) return;
       ++sc;
       tc_fence_after();
+      BW_TRACE_AT(t == 0, 10 + w, sc - 1);
       uint32_t r[128];
       tmem_ld128(s_tmem, r);
       float* s = reinterpret_cast<float*>(r);
@@ -318,6 +334,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
           for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
         mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
       }
+      BW_TRACE_AT(t == 0, 14 + w, sc - 1);
       const float m_cand = mx * c;
       float corr = 1.f;
       const bool upd = m_cand > m_run + 8.f;
@@ -334,6 +351,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
         s[2 * k] = x.x;
         s[2 * k + 1] = x.y;
       }
+      BW_TRACE_AT(t == 0, 16 + w, sc - 1);
       // Phase 2: exponentials in place; POLY of every 8 pairs on the FMA pipe.
 #pragma unroll
       for (int k = 0; k < 64; ++k) {
@@ -346,6 +364,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
           s[2 * k + 1] = ex2_mufu(s[2 * k + 1]);
         }
       }
+      BW_TRACE_AT(t == 0, 18 + w, sc - 1);
       // Phase 3: row sum (four paired accumulators) and bf16 packing.
       f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
 #pragma unroll
@@ -360,6 +379,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
       for (int k = 0; k < 64; ++k) pk[k] = pack_bf16(s[2 * k], s[2 * k + 1]);
       acc0 = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
       l_run = l_run * corr + (acc0.x + acc0.y);
+      BW_TRACE_AT(t == 0, 30 + w, sc - 1);
       if constexpr (PT) {
         tmem_st32(s_tmem, pk);
         tmem_st32(s_tmem + 32, pk + 32);
@@ -386,6 +406,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
       if constexpr (!PT) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       mbar_arrive(&bars.p_full[w]);
+      BW_TRACE_AT(t == 0, 40 + w, sc - 1);
     }
     if (!wc.wait(&bars.o_full[w], oc & 1)) return;
     ++oc;
@@ -413,10 +434,18 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
   }
 }
 
+struct Roles {
+  static constexpr int kSoftThreads = 128;   // per warpgroup
+  static constexpr int kProducerWarp = 2 * kSoftThreads / 32;
+  static constexpr int kMmaWarp = kProducerWarp + 1;
+  static constexpr int kThreads = 32 * (kMmaWarp + 1);
+};
+
 template <int D, bool PT, int POLY>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Roles::kThreads, 1)
     fmha_fwd_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
   using L = Layout<D, PT>;
+  using R = Roles;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars& bars = *reinterpret_cast<Bars*>(smem + L::kBar);
@@ -429,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.q_full[w], 1);
       mbar_init(&bars.q_empty[w], 1);
       mbar_init(&bars.s_full[w], 1);
-      mbar_init(&bars.p_full[w], 128);
+      mbar_init(&bars.p_full[w], R::kSoftThreads);
       mbar_init(&bars.o_full[w], 1);
     }
     mbar_init(&bars.mma_done, 1);
@@ -440,28 +469,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars.abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == R::kProducerWarp && lane == 0) {
     prefetch_tmap(&maps.q);
     prefetch_tmap(&maps.k);
     prefetch_tmap(&maps.v);
   }
-  if (warp == 9) tmem_alloc(&bars.tmem_base, 512);
+  if (warp == R::kMmaWarp) tmem_alloc(&bars.tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars.tmem_base;
   WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, warp};
 
-  if (warp < 8) {
-    softmax_role<D, PT, POLY>(p, smem, bars, wc, tmem, warp >> 2, tid & 127);
-  } else if (warp == 8) {
+  if (warp < R::kProducerWarp) {
+    const int w = tid / R::kSoftThreads;
+    softmax_role<D, PT, POLY>(p, smem, bars, wc, tmem, w, tid % R::kSoftThreads);
+  } else if (warp == R::kProducerWarp) {
     if (lane == 0) producer_role<D, PT>(p, maps, smem, bars, wc);
   } else {
     if (lane == 0) mma_role<D, PT>(p, smem, bars, wc, tmem);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == R::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -470,6 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D, bool PT, int POLY>
 cudaError_t launch_impl(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
   constexpr int bytes = Layout<D, PT>::kBytes + 1024;
+  constexpr int kThreads = Roles::kThreads;
   auto kern = fmha_fwd_kernel<D, PT, POLY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
@@ -501,3 +532,10 @@ cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in
 }
 
 }  // namespace bw
+
+#ifdef BW_TRACE
+extern "C" __attribute__((visibility("default"))) int bw_trace_read(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, g_bw_trace, sizeof(g_bw_trace));
+  return 64 * 512;
+}
+#endif

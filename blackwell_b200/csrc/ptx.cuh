@@ -8,6 +8,22 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+// Optional timeline probes, compiled only with -DBW_TRACE (never in the shipped
+// library): slot (ev, idx) of CTA 0 receives clock64() with a plain store, so a
+// probe adds only a few cycles to the interval it measures.
+#ifdef BW_TRACE
+__device__ unsigned long long g_bw_trace[64 * 512];
+#define BW_TRACE_AT(cond, ev, idx)                                  \
+  do {                                                              \
+    if ((cond) && blockIdx.x == 0 && (idx) < 512)                   \
+      g_bw_trace[(ev) * 512 + (idx)] = clock64();                   \
+  } while (0)
+#else
+#define BW_TRACE_AT(cond, ev, idx) \
+  do {                             \
+  } while (0)
+#endif
+
 namespace bw {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -141,6 +157,35 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accum)
       : "memory");
 }
+
+// Same MMAs with each 64-bit shared-memory descriptor passed as (lo, hi)
+// 32-bit halves: only the low half (start address) changes between the
+// K-steps of a tile, so the issuing thread advances it with one 32-bit add.
+__device__ __forceinline__ void mma_ss_lh(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                          uint32_t b_hi, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_lh(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                          uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Halves of sdesc_sw128(saddr, lbo, 1024).
+__device__ __forceinline__ uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo) {
+  return ((saddr & 0x3FFFFu) >> 4) | ((lbo >> 4) << 16);
+}
+__host__ __device__ constexpr uint32_t sdesc_hi_sbo1024() { return (1024u >> 4) | (1u << 14) | (2u << 29); }
 
 // Instruction descriptor, kind::f16: D=f32 (bits 4-5 = 1), A=B=bf16 (bits 7-9,
 // 10-12 = 1), A K-major, B K-major or MN-major (bit 16), N>>3 at bit 17, M>>4 at

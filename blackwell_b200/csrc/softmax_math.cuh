@@ -22,6 +22,11 @@ struct f2 {
   float x, y;
 };
 
+#ifdef BW_SCALAR_F2
+__device__ __forceinline__ f2 ffma2(f2 a, f2 b, f2 c) { return f2{fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y)}; }
+__device__ __forceinline__ f2 fadd2(f2 a, f2 b) { return f2{a.x + b.x, a.y + b.y}; }
+__device__ __forceinline__ f2 fsub2(f2 a, f2 b) { return f2{a.x - b.x, a.y - b.y}; }
+#else
 __device__ __forceinline__ f2 ffma2(f2 a, f2 b, f2 c) {
   f2 d;
   asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
@@ -49,6 +54,7 @@ __device__ __forceinline__ f2 fsub2(f2 a, f2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
+#endif
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

@@ -140,7 +140,13 @@ BW_API int bw_stream_status(void* stream);
  *   BW_OPT_EXP_POLY        of every 8 pairs of softmax exponentials, how many
  *                          are computed by an FMA-pipe polynomial instead of
  *                          MUFU ex2: 0, 2 (default), 3 or 4 */
-enum { BW_OPT_TIMEOUT_NS = 1, BW_OPT_P_IN_TMEM = 2, BW_OPT_DEBUG_FLAGS = 3, BW_OPT_MAX_CTAS = 4, BW_OPT_EXP_POLY = 5 };
+enum {
+  BW_OPT_TIMEOUT_NS = 1,
+  BW_OPT_P_IN_TMEM = 2,
+  BW_OPT_DEBUG_FLAGS = 3,
+  BW_OPT_MAX_CTAS = 4,
+  BW_OPT_EXP_POLY = 5
+};
 BW_API int bw_set_option(int key, int64_t value);
 BW_API int64_t bw_get_option(int key);
 

@@ -18,6 +18,7 @@ GOLDEN_GQA = ["gqa_nc_d128", "gqa_causal_d128", "gqa_causal_d64_g3_rand", "gqa_c
 
 @pytest.fixture(scope="module", params=[1, 0], ids=["p_tmem", "p_smem"])
 def p_variant(request):
+    """Kernel variants: P fed to the PV MMA from TMEM or from shared memory."""
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
     old = bw.get_option(_ffi.BW_OPT_P_IN_TMEM)
