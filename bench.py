@@ -235,11 +235,12 @@ def time_steps(fn, steps, warmup, flush, world):
     return [a.elapsed_time(b) for a, b in evs]
 
 
-def bench_decode(flush, steps, warmup):
-    """C4: split-KV decode B=64, Hq=64, Hkv=8, D=128, L_b ~ U[1024, 32768] (seed 42)."""
+def bench_decode(flush, steps, warmup, len_div=1):
+    """C4: split-KV decode B=64, Hq=64, Hkv=8, D=128, L_b ~ U[1024, 32768] (seed 42).
+    len_div > 1 divides every length (small case for profiler captures)."""
     import blackwell_b200 as bw
     B, Hq, Hkv, D = 64, 64, 8, 128
-    lens = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(42))
+    lens = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(42)) // len_div
     total = int(lens.sum())
     offs = torch.cumsum(lens, 0) - lens
     g = torch.Generator(device="cuda").manual_seed(42)
@@ -377,6 +378,20 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_single(args):
+    """One workload's kernel, W warm-up + K timed steps (for ncu captures)."""
+    torch.cuda.set_device(0)
+    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    flush = lambda: flush_buf.zero_()
+    shapes = {"c2": ((4, 32, 8, 4096, 128), True, "bshd"), "c3d64": ((8, 16, 16, 2048, 64), False, "bhsd"),
+              "c3d128": ((8, 16, 16, 2048, 128), False, "bhsd"), "refshape": ((8, 12, 4, 4096, 64), True, "bhsd")}
+    if args.workload in shapes:
+        r = bench_prefill(*shapes[args.workload], flush, args.steps, args.warmup)
+    else:
+        r = bench_decode(flush, args.steps, args.warmup, len_div=8 if args.workload == "c4small" else 1)
+    print(json.dumps({"workload": args.workload, **r}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -386,7 +401,12 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="short run for profiler captures: no secondary configs, no CPU baseline")
+    ap.add_argument("--workload", choices=["c2", "c3d64", "c3d128", "c4", "c4small", "refshape"], default=None,
+                    help="profiler aid: run only this workload's kernel and print its timing")
     args = ap.parse_args()
+    if args.workload:
+        run_single(args)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_setup()
