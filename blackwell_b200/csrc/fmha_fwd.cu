@@ -334,7 +334,6 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
           for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
         mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
       }
-      BW_TRACE_AT(t == 0, 14 + w, sc - 1);
       const float m_cand = mx * c;
       float corr = 1.f;
       const bool upd = m_cand > m_run + 8.f;
@@ -351,7 +350,6 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
         s[2 * k] = x.x;
         s[2 * k + 1] = x.y;
       }
-      BW_TRACE_AT(t == 0, 16 + w, sc - 1);
       // Phase 2: exponentials in place; POLY of every 8 pairs on the FMA pipe.
 #pragma unroll
       for (int k = 0; k < 64; ++k) {
@@ -364,7 +362,6 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
           s[2 * k + 1] = ex2_mufu(s[2 * k + 1]);
         }
       }
-      BW_TRACE_AT(t == 0, 18 + w, sc - 1);
       // Phase 3: row sum (four paired accumulators) and bf16 packing.
       f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
 #pragma unroll
