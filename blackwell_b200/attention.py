@@ -169,3 +169,32 @@ def shard_plan(units: int, world: int, rank: int):
     b, e = ctypes.c_int64(), ctypes.c_int64()
     _ffi.check(_ffi.lib().bw_shard_plan(units, world, rank, ctypes.byref(b), ctypes.byref(e)), "bw_shard_plan")
     return b.value, e.value
+
+
+def gqa_decode_partial(q, k, v, kv_lens, kv_offsets, scale=None, chunk=0, workspace=None, out=None, lse=None):
+    """Split-KV decode over this GPU's keys only, leaving fp32 partials for a merge:
+    returns (O fp32 [B,Hq,D] normalised by its own sum, LSE fp32 [B,Hq], -inf where
+    a sequence has no local keys)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+    if kv_lens.dtype != torch.int32 or kv_offsets.dtype != torch.int64:
+        raise TypeError("kv_lens must be int32 and kv_offsets int64")
+    B, Hq, D = q.shape
+    total, Hkv, _ = k.shape
+    if total == 0:  # no local keys at all: the neutral partial of the LSE merge
+        return (torch.zeros((B, Hq, D), dtype=torch.float32, device=q.device),
+                torch.full((B, Hq), float("-inf"), dtype=torch.float32, device=q.device))
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if workspace is None:
+        workspace = torch.empty(decode_workspace_size(B, Hq, Hkv, D, total, chunk), dtype=torch.uint8,
+                                device=q.device)
+    o = out if out is not None else torch.empty((B, Hq, D), dtype=torch.float32, device=q.device)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    rc = _ffi.lib().bw_gqa_decode_partial(_ptr(q), _ptr(k), _ptr(v), _ptr(kv_lens), _ptr(kv_offsets), _ptr(o),
+                                          _ptr(lse), B, Hq, Hkv, D, int(total), float(scale), int(chunk),
+                                          _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())
+    _ffi.check(rc, "bw_gqa_decode_partial")
+    return o, lse

@@ -209,8 +209,8 @@ size_t bw_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int64_t total
   return align256((size_t)(B + 1) * 4) + align256((size_t)parts * G * 4) + (size_t)parts * G * D * 4;
 }
 
-int bw_gqa_decode(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets,
-                  void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
+static int decode_impl(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets,
+                  void* O, int o_fp32, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
                   void* workspace, size_t workspace_bytes, void* stream) {
   if (!Q || !K || !V || !kv_lens || !kv_offsets || !O || !workspace) return BW_ERR_NULL;
   if (B <= 0 || B > 4096 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0) return BW_ERR_SHAPE;
@@ -277,8 +277,25 @@ int bw_gqa_decode(const void* Q, const void* K, const void* V, const int* kv_len
   c.o_sb = (int64_t)Hq * D;
   c.o_sh = D;
   c.LSE = LSE;
+  c.o_fp32 = o_fp32;
   e = bw::launch_lse_combine(c, s);
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
+}
+
+int bw_gqa_decode(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets,
+                  void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_impl(Q, K, V, kv_lens, kv_offsets, O, 0, LSE, B, Hq, Hkv, D, total_tokens, scale, chunk, workspace,
+                     workspace_bytes, stream);
+}
+
+int bw_gqa_decode_partial(const void* Q, const void* K, const void* V, const int* kv_lens,
+                          const int64_t* kv_offsets, float* O, float* LSE, int B, int Hq, int Hkv, int D,
+                          int64_t total_tokens, float scale, int chunk, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  if (!LSE) return BW_ERR_NULL;
+  return decode_impl(Q, K, V, kv_lens, kv_offsets, O, 1, LSE, B, Hq, Hkv, D, total_tokens, scale, chunk, workspace,
+                     workspace_bytes, stream);
 }
 
 int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
@@ -300,6 +317,7 @@ int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B
   c.o_sb = (int64_t)Hq * D;
   c.o_sh = D;
   c.LSE = LSE;
+  c.o_fp32 = 0;
   cudaError_t e = bw::launch_lse_combine(c, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }

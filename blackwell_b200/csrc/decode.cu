@@ -364,9 +364,14 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(const CombineParams p)
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   if (d0 < p.D) {
-    __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(p.O) + b * p.o_sb + hq * p.o_sh + d0;
-    uint2 u = make_uint2(pack2(accv[0] * inv, accv[1] * inv), pack2(accv[2] * inv, accv[3] * inv));
-    *reinterpret_cast<uint2*>(O) = u;
+    if (p.o_fp32) {
+      float* O = reinterpret_cast<float*>(p.O) + b * p.o_sb + hq * p.o_sh + d0;
+      *reinterpret_cast<float4*>(O) = make_float4(accv[0] * inv, accv[1] * inv, accv[2] * inv, accv[3] * inv);
+    } else {
+      __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(p.O) + b * p.o_sb + hq * p.o_sh + d0;
+      uint2 u = make_uint2(pack2(accv[0] * inv, accv[1] * inv), pack2(accv[2] * inv, accv[3] * inv));
+      *reinterpret_cast<uint2*>(O) = u;
+    }
   }
   if (p.LSE && lane == 0) p.LSE[(int64_t)b * p.Hq + hq] = wsum > 0.f ? msafe + __logf(wsum) : -INFINITY;
 }

@@ -152,6 +152,7 @@ int bw_gqa_decode_static(const void* Q, const void* K, const void* V, const int*
   c.o_sb = (int64_t)Hq * D;
   c.o_sh = D;
   c.LSE = LSE;
+  c.o_fp32 = 0;
   return bw::launch_lse_combine(c, s) == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 

@@ -65,6 +65,7 @@ struct CombineParams {
   void* O;                       // bf16 [B, Hq, D] (strides o_sb, o_sh)
   int64_t o_sb, o_sh;
   float* LSE;                    // fp32 [B, Hq], may be null
+  int o_fp32;                    // 1: O is fp32 (strides in fp32 elements) instead of bf16
 };
 
 cudaError_t launch_lse_combine(const CombineParams& p, cudaStream_t stream);

@@ -102,6 +102,18 @@ BW_API int bw_gqa_decode(const void* Q, const void* K, const void* V, const int*
                   void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Split-KV decode that leaves fp32 partial results for a cross-GPU merge (new;
+ * no reference counterpart).  Same arguments as bw_gqa_decode, but O is fp32
+ * [B, Hq, D] normalised by this call's own softmax sum and LSE (required) is
+ * the natural-log sum over this call's keys (-inf for an empty sequence).  When
+ * each GPU holds a slice of every sequence's KV, every GPU runs this on its
+ * slice, the partials are all-gathered into [world, B, Hq, D] / [world, B, Hq]
+ * and bw_lse_combine merges them. */
+BW_API int bw_gqa_decode_partial(const void* Q, const void* K, const void* V, const int* kv_lens,
+                                 const int64_t* kv_offsets, float* O, float* LSE, int B, int Hq, int Hkv, int D,
+                                 int64_t total_tokens, float scale, int chunk, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* The same decode for callers that cannot allocate device memory (no
  * counterpart in the reference: it is an addition of this library).  Callers
  * such as allocator hooks, memory-pool callbacks or host runtimes that own no
