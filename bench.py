@@ -283,6 +283,40 @@ def bench_prefill(shape, causal, layout, flush, steps, warmup):
     return {"ms": t, "TFLOP/s": flops / t / 1e9}
 
 
+def bench_c5(world, rank, steps, warmup):
+    """C5: causal GQA B=1, Hq=64, Hkv=8, S=131072, D=128, one or more KV-head groups
+    per rank (8 groups sharded over the ranks, no exchange).  Each rank holds only
+    its groups' Q/K/V (BHSD).  Time = max over ranks of the CUDA-event time."""
+    import blackwell_b200 as bw
+    from blackwell_b200.distributed import unit_range
+    Hq, Hkv, S, D = 64, 8, 131072, 128
+    G = Hq // Hkv
+    g0, g1 = unit_range(Hkv, world, rank)
+    ng = g1 - g0
+    if ng == 0:
+        ms = 0.0
+    else:
+        gen = torch.Generator(device="cuda").manual_seed(42 + rank)
+        q = torch.randn(1, ng * G, S, D, generator=gen, device="cuda").bfloat16()
+        k = torch.randn(1, ng, S, D, generator=gen, device="cuda").bfloat16()
+        v = torch.randn(1, ng, S, D, generator=gen, device="cuda").bfloat16()
+        o = torch.empty_like(q)
+        lse = torch.empty(1, ng * G, S, dtype=torch.float32, device="cuda")
+        fn = lambda: bw.gqa_causal_fwd(q, k, v, out=o, lse=lse)
+        ms = statistics.median(time_steps(fn, steps, warmup, lambda: None, world))
+        assert bw.stream_status() == 0
+        del q, k, v, o
+        torch.cuda.empty_cache()
+    if ng == 0:
+        time_steps(lambda: None, steps, warmup, lambda: None, world)
+    ms_max = max_over_ranks(ms, world)
+    flops = causal_flops(1, Hq, S, D)
+    return {"workload": "C5 causal GQA B=1 Hq=64 Hkv=8 S=131072 D=128, KV groups sharded over ranks",
+            "groups_per_rank": [unit_range(Hkv, world, r)[1] - unit_range(Hkv, world, r)[0] for r in range(world)],
+            "ms": ms_max, "TFLOP/s_total": flops / ms_max / 1e9, "TFLOP/s_per_gpu": flops / ms_max / 1e9 / world,
+            "l2": "inputs (>= 320 MiB per rank) exceed L2; no flush"}
+
+
 def run_ours(args, world, rank, local):
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
@@ -350,6 +384,12 @@ def run_ours(args, world, rank, local):
         dec = bench_decode(flush, sec_steps, 3)
         dec["frac_of_hbm_peak"] = dec["GB/s"] / peaks["hbm_gbs"]
         secondary["C4_decode"] = dec
+
+    if not (args.no_secondary or args.profile):
+        c5 = bench_c5(world, rank, 3, 3)
+        if rank == 0:
+            c5["frac_of_peak_per_gpu"] = c5["TFLOP/s_per_gpu"] / peaks["bf16_tflops"]
+            secondary["C5_long_context"] = c5
 
     cpu = None
     if rank == 0 and world == 1 and not args.profile:

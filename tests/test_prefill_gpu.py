@@ -158,3 +158,25 @@ def test_exp_poly_split(golden, name, poly):
     assert np.abs(o - g["o_fp64"]).max() <= O_TOL
     assert np.abs(o - g["o_fp64"]).mean() <= 2e-3
     assert np.abs(lse - g["lse_fp64"]).max() <= LSE_TOL
+
+
+def test_long_context_rows():
+    """C5's per-GPU slice shape (one KV group: Hq=8 query heads, Hkv=1, D=128,
+    causal) at S = 65536: 160 rows (including the first and last tiles) against
+    the fp64 row oracle."""
+    import blackwell_b200 as bw
+    B, Hq, Hkv, S, D = 1, 8, 1, 65536, 128
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn(B, Hq, S, D, generator=g, device="cuda").bfloat16()
+    k = torch.randn(B, Hkv, S, D, generator=g, device="cuda").bfloat16()
+    v = torch.randn(B, Hkv, S, D, generator=g, device="cuda").bfloat16()
+    o, lse = bw.gqa_causal_fwd(q, k, v)
+    assert bw.stream_status() == 0
+    rng = np.random.default_rng(11)
+    rows = np.stack([np.zeros(160, int), rng.integers(0, Hq, 160), rng.integers(0, S, 160)], 1)
+    rows[:6, 2] = [0, 127, 128, S - 129, S - 128, S - 1]
+    qc, kc, vc = q.float().cpu(), k.float().cpu(), v.float().cpu()
+    ro, rl = orc.fp64_rows(qc, kc, vc, 1 / math.sqrt(D), True, rows)
+    oc, lc = o.float().cpu().numpy(), lse.cpu().numpy()
+    assert np.abs(np.stack([oc[b, h, i] for b, h, i in rows]) - ro).max() <= O_TOL
+    assert np.abs(np.array([lc[b, h, i] for b, h, i in rows]) - rl).max() <= LSE_TOL
