@@ -31,6 +31,8 @@ SIGNATURES = {
     "bw_mha_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _SP, _vp]),
     "bw_gqa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i64, _i]),
     "bw_gqa_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _f, _i, _vp, _sz, _vp]),
+    "bw_gqa_decode_paged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _sz,
+                                 _vp]),
     "bw_gqa_decode_partial": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _f, _i, _vp, _sz, _vp]),
     "bw_gqa_decode_static_scratch_bytes": (_sz, []),
     "bw_gqa_decode_static": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _f, _i, _vp]),

@@ -198,3 +198,37 @@ def gqa_decode_partial(q, k, v, kv_lens, kv_offsets, scale=None, chunk=0, worksp
                                           _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())
     _ffi.check(rc, "bw_gqa_decode_partial")
     return o, lse
+
+
+def gqa_decode_paged(q, k_cache, v_cache, block_table, kv_lens, scale=None, chunk=0, workspace=None, out=None,
+                     lse=None):
+    """Split-KV decode over a paged KV cache.
+
+    q [B, Hq, D] bf16; k_cache / v_cache [num_pages, page_size, Hkv, D] bf16;
+    block_table int32 [B, max_pages_per_seq]; kv_lens int32 [B].
+    Returns (O [B, Hq, D] bf16, LSE [B, Hq] fp32)."""
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+    if block_table.dtype != torch.int32 or kv_lens.dtype != torch.int32 or not block_table.is_contiguous():
+        raise TypeError("block_table and kv_lens must be contiguous int32")
+    B, Hq, D = q.shape
+    num_pages, page_size, Hkv, Dk = k_cache.shape
+    if Dk != D or v_cache.shape != k_cache.shape or block_table.shape[0] != B or kv_lens.numel() != B:
+        raise ValueError("shape mismatch")
+    max_pages = block_table.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    bound = min(num_pages * page_size, B * max_pages * page_size)
+    if workspace is None:
+        workspace = torch.empty(decode_workspace_size(B, Hq, Hkv, D, bound, chunk), dtype=torch.uint8,
+                                device=q.device)
+    o = out if out is not None else torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    rc = _ffi.lib().bw_gqa_decode_paged(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(block_table), _ptr(kv_lens),
+                                        _ptr(o), _ptr(lse), B, Hq, Hkv, D, page_size, num_pages, max_pages,
+                                        float(scale), int(chunk), _ptr(workspace),
+                                        workspace.numel() * workspace.element_size(), _stream())
+    _ffi.check(rc, "bw_gqa_decode_paged")
+    return o, lse

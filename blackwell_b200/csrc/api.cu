@@ -75,10 +75,10 @@ int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, 
 }
 
 // 2-D map over [rows, cols] bf16 (row stride = cols), box (64, 64), 128B swizzle.
-int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
+int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint32_t box_rows = 64) {
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {64, box_rows};
   cuuint32_t es[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -296,6 +296,86 @@ int bw_gqa_decode_partial(const void* Q, const void* K, const void* V, const int
   if (!LSE) return BW_ERR_NULL;
   return decode_impl(Q, K, V, kv_lens, kv_offsets, O, 1, LSE, B, Hq, Hkv, D, total_tokens, scale, chunk, workspace,
                      workspace_bytes, stream);
+}
+
+int bw_gqa_decode_paged(const void* Q, const void* K_cache, const void* V_cache, const int* block_table,
+                        const int* kv_lens, void* O, float* LSE, int B, int Hq, int Hkv, int D, int page_size,
+                        int num_pages, int max_pages_per_seq, float scale, int chunk, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!Q || !K_cache || !V_cache || !block_table || !kv_lens || !O || !workspace) return BW_ERR_NULL;
+  if (B <= 0 || B > 4096 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0) return BW_ERR_SHAPE;
+  const int G = Hq / Hkv;
+  if (G > 16 || (D != 64 && D != 128) || num_pages <= 0 || max_pages_per_seq <= 0) return BW_ERR_SHAPE;
+  // page pieces must start on 1024-byte (8-row) boundaries of the swizzled stage
+  const bool ps_ok = page_size >= 8 && ((page_size <= 64 && 64 % page_size == 0) || page_size % 64 == 0);
+  if (!ps_ok) return BW_ERR_SHAPE;
+  const int64_t rows = (int64_t)num_pages * page_size;
+  if (rows >= (int64_t(1) << 31)) return BW_ERR_SHAPE;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return BW_ERR_SHAPE;
+  if (chunk <= 0) chunk = kDefaultChunk;
+  if (chunk % 64 != 0) return BW_ERR_SHAPE;
+  if (!aligned16(Q) || !aligned16(K_cache) || !aligned16(V_cache) || !aligned16(O) || !aligned16(workspace))
+    return BW_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(block_table) & 3u) || (reinterpret_cast<uintptr_t>(kv_lens) & 3u))
+    return BW_ERR_ALIGN;
+  const int64_t max_tokens = (int64_t)B * max_pages_per_seq * page_size;
+  const int64_t bound = max_tokens < rows ? max_tokens : rows;
+  if (workspace_bytes < bw_gqa_decode_workspace_size(B, Hq, Hkv, D, bound, chunk)) return BW_ERR_WORKSPACE;
+
+  DeviceState* dev = nullptr;
+  int rc = get_device_state(&dev);
+  if (rc != BW_OK) return rc;
+  const uint32_t box_rows = page_size < 64 ? (uint32_t)page_size : 64u;
+  bw::DecodeMaps maps;
+  if (make_map_2d(&maps.k, K_cache, rows, (int64_t)Hkv * D, box_rows) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_2d(&maps.v, V_cache, rows, (int64_t)Hkv * D, box_rows) != BW_OK) return BW_ERR_CUDA;
+
+  const int64_t parts = decode_max_parts(B, Hkv, bound, chunk);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* prefix = reinterpret_cast<int*>(ws);
+  float* lse_part = reinterpret_cast<float*>(ws + align256((size_t)(B + 1) * 4));
+  float* o_part = reinterpret_cast<float*>(ws + align256((size_t)(B + 1) * 4) + align256((size_t)parts * G * 4));
+
+  bw::DecodeParams p{};
+  p.Q = Q;
+  p.q_sb = (int64_t)Hq * D;
+  p.q_sh = D;
+  p.kv_lens = kv_lens;
+  p.kv_offsets = nullptr;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = G;
+  p.D = D;
+  p.chunk = chunk;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o_part = o_part;
+  p.lse_part = lse_part;
+  p.chunk_prefix = prefix;
+  p.max_parts = (int)parts;
+  p.err = dev->err;
+  p.timeout_ns = (uint64_t)g_timeout_ns.load();
+  p.block_table = block_table;
+  p.page_size = page_size;
+  p.max_pages = max_pages_per_seq;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bw::launch_decode(p, maps, dev->num_sms, s) != cudaSuccess) return BW_ERR_CUDA;
+
+  bw::CombineParams c{};
+  c.o_part = o_part;
+  c.lse_part = lse_part;
+  c.chunk_prefix = prefix;
+  c.B = B;
+  c.Hq = Hq;
+  c.Hkv = Hkv;
+  c.G = G;
+  c.D = D;
+  c.O = O;
+  c.o_sb = (int64_t)Hq * D;
+  c.o_sh = D;
+  c.LSE = LSE;
+  c.o_fp32 = 0;
+  return bw::launch_lse_combine(c, s) == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
 int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,

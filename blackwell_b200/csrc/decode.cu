@@ -93,7 +93,7 @@ __device__ __forceinline__ DecItem dec_item(const DecodeParams& p, const int* pr
   it.b = lo;
   it.c = pc - prefix[lo];
   it.part = idx;
-  const int64_t base = p.kv_offsets[it.b];
+  const int64_t base = p.block_table ? 0 : p.kv_offsets[it.b];   // paged: sequence-relative tokens
   const int len = p.kv_lens[it.b];
   it.t0 = base + (int64_t)it.c * p.chunk;
   const int64_t end = base + len;
@@ -149,6 +149,8 @@ __global__ void __launch_bounds__(kThreads)
       uint32_t n = 0;
       for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
         const DecItem it = dec_item(p, prefix, idx);
+        const int len_b = p.kv_lens[it.b];
+        const int* bt_b = p.block_table ? p.block_table + (int64_t)it.b * p.max_pages : nullptr;
         for (int64_t t = it.t0; t < it.t1; t += kTok, ++n) {
           const uint32_t s = n % kStages;
           if (!wc.wait(&bars.empty[s], ((n / kStages) & 1) ^ 1)) {
@@ -159,10 +161,30 @@ __global__ void __launch_bounds__(kThreads)
           }
           mbar_arrive_expect_tx(&bars.full[s], C::kStage);
           uint8_t* dst = smem + s * C::kStage;
+          if (p.block_table == nullptr) {
 #pragma unroll
-          for (int pn = 0; pn < D / 64; ++pn) {
-            tma_load_2d(dst + pn * C::kPanel, &maps.k, &bars.full[s], it.kvh * D + pn * 64, (int)t);
-            tma_load_2d(dst + C::kHalf + pn * C::kPanel, &maps.v, &bars.full[s], it.kvh * D + pn * 64, (int)t);
+            for (int pn = 0; pn < D / 64; ++pn) {
+              tma_load_2d(dst + pn * C::kPanel, &maps.k, &bars.full[s], it.kvh * D + pn * 64, (int)t);
+              tma_load_2d(dst + C::kHalf + pn * C::kPanel, &maps.v, &bars.full[s], it.kvh * D + pn * 64, (int)t);
+            }
+          } else {
+            // Paged: the 64-token stage is gathered page piece by page piece
+            // (bh = min(64, page_size) rows per box).  Pieces past the end of the
+            // sequence re-read its last piece (in range; masked by the consumers).
+            const int bh = p.page_size < kTok ? p.page_size : kTok;
+            const int last = ((len_b - 1) / bh) * bh;
+            for (int sub = 0; sub < kTok / bh; ++sub) {
+              int tok = (int)t + sub * bh;
+              if (tok > last) tok = last;
+              const int page = bt_b[tok / p.page_size];
+              const int row = page * p.page_size + tok % p.page_size;
+#pragma unroll
+              for (int pn = 0; pn < D / 64; ++pn) {
+                tma_load_2d(dst + pn * C::kPanel + sub * bh * 128, &maps.k, &bars.full[s], it.kvh * D + pn * 64, row);
+                tma_load_2d(dst + C::kHalf + pn * C::kPanel + sub * bh * 128, &maps.v, &bars.full[s],
+                            it.kvh * D + pn * 64, row);
+              }
+            }
           }
         }
       }

@@ -33,16 +33,17 @@
 #include "../../include/bw_attn.h"
 #include "kernels.h"
 
-namespace {
-
 constexpr size_t kStaticScratchBytes = size_t(32) << 20;
-constexpr int kDefaultChunk = 1024;
-constexpr int kMaxDevices = 64;
 
 // The scratch itself.  In host code this name is only a stand-in for the
 // symbol, not a device address: a kernel must be given the address returned by
 // cudaGetSymbolAddress for the current device.
-__device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+
+namespace {
+constexpr int kDefaultChunk = 1024;
+constexpr int kMaxDevices = 64;
+
 
 std::mutex g_static_mu;
 void* g_scratch_addr[kMaxDevices] = {};

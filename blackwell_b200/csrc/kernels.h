@@ -47,10 +47,14 @@ struct DecodeParams {
   int max_parts;                 // capacity of o_part / lse_part (bounds check)
   int* err;
   uint64_t timeout_ns;
+  // Paged KV cache (block_table != null): K/V rows are page * page_size + slot,
+  // token i of sequence b lives in page block_table[b * max_pages + i / page_size].
+  const int* block_table;
+  int page_size, max_pages;
 };
 
 struct DecodeMaps {
-  CUtensorMap k, v;              // 2-D (Hkv*D, total_tokens) bf16, box (64, 64), SWIZZLE_128B
+  CUtensorMap k, v;              // 2-D (Hkv*D, rows) bf16, box (64, min(64, page_size)), SWIZZLE_128B
 };
 
 cudaError_t launch_decode(const DecodeParams& p, const DecodeMaps& maps, int num_sms, cudaStream_t stream);

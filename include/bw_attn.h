@@ -102,6 +102,20 @@ BW_API int bw_gqa_decode(const void* Q, const void* K, const void* V, const int*
                   void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Split-KV decode over a paged KV cache (new; no reference counterpart -- the
+ * closest relative is the reference's split-length launcher, adhitya_GQA.cu:50-55).
+ *   K_cache, V_cache: bf16 [num_pages, page_size, Hkv, D] contiguous
+ *   block_table: int32 [B, max_pages_per_seq]; token i of sequence b is slot
+ *                i % page_size of page block_table[b][i / page_size]
+ *   kv_lens: int32 [B];  Q, O, LSE as in bw_gqa_decode.
+ * page_size: 8, 16, 32, 64 or any multiple of 64.  Workspace:
+ * bw_gqa_decode_workspace_size(B, Hq, Hkv, D, min(num_pages * page_size,
+ * B * max_pages_per_seq * page_size), chunk) bytes. */
+BW_API int bw_gqa_decode_paged(const void* Q, const void* K_cache, const void* V_cache, const int* block_table,
+                               const int* kv_lens, void* O, float* LSE, int B, int Hq, int Hkv, int D, int page_size,
+                               int num_pages, int max_pages_per_seq, float scale, int chunk, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Split-KV decode that leaves fp32 partial results for a cross-GPU merge (new;
  * no reference counterpart).  Same arguments as bw_gqa_decode, but O is fp32
  * [B, Hq, D] normalised by this call's own softmax sum and LSE (required) is
