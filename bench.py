@@ -261,6 +261,41 @@ def bench_decode(flush, steps, warmup, len_div=1):
             "sum_L": total, "ms": t, "GB/s": nbytes / t / 1e6, "algorithmic_bytes": nbytes, "launches_per_step": 2}
 
 
+def bench_decode_paged(flush, steps, warmup, page_size=64):
+    """C4 over a paged KV cache: the same lengths, K/V in pages of `page_size`
+    tokens placed in a random physical order (seed 42)."""
+    import blackwell_b200 as bw
+    B, Hq, Hkv, D = 64, 64, 8, 128
+    lens = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(42))
+    pages = (lens + page_size - 1) // page_size
+    num_pages = int(pages.sum())
+    max_pages = int(pages.max())
+    perm = torch.randperm(num_pages, generator=torch.Generator().manual_seed(42)).int()
+    bt = torch.full((B, max_pages), -1, dtype=torch.int32)
+    start = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[start:start + pages[b]]
+        start += int(pages[b])
+    g = torch.Generator(device="cuda").manual_seed(42)
+    q = torch.randn(B, Hq, D, generator=g, device="cuda").bfloat16()
+    kc = torch.randn(num_pages, page_size, Hkv, D, generator=g, device="cuda").bfloat16()
+    vc = torch.randn(num_pages, page_size, Hkv, D, generator=g, device="cuda").bfloat16()
+    bt_d, lens_d = bt.cuda(), lens.int().cuda()
+    o = torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, Hq, dtype=torch.float32, device="cuda")
+    bound = min(num_pages * page_size, B * max_pages * page_size)
+    ws = torch.empty(bw.attention.decode_workspace_size(B, Hq, Hkv, D, bound), dtype=torch.uint8, device="cuda")
+    fn = lambda: bw.attention.gqa_decode_paged(q, kc, vc, bt_d, lens_d, workspace=ws, out=o, lse=lse)
+    ms = time_steps(fn, steps, warmup, flush, 1)
+    assert bw.stream_status() == 0
+    total = int(lens.sum())
+    nbytes = 2 * total * Hkv * D * 2 + 2 * B * Hq * D * 2 + B * Hq * 4
+    t = statistics.median(ms)
+    del kc, vc
+    return {"workload": f"C4 over a paged KV cache, page_size {page_size}, pages in random order",
+            "ms": t, "GB/s": nbytes / t / 1e6}
+
+
 def bench_prefill(shape, causal, layout, flush, steps, warmup):
     import blackwell_b200 as bw
     B, Hq, Hkv, S, D = shape
@@ -384,6 +419,10 @@ def run_ours(args, world, rank, local):
         dec = bench_decode(flush, sec_steps, 3)
         dec["frac_of_hbm_peak"] = dec["GB/s"] / peaks["hbm_gbs"]
         secondary["C4_decode"] = dec
+        for ps in (16, 64):
+            dp = bench_decode_paged(flush, sec_steps, 3, page_size=ps)
+            dp["frac_of_hbm_peak"] = dp["GB/s"] / peaks["hbm_gbs"]
+            secondary[f"C4_decode_paged_{ps}"] = dp
 
     if not (args.no_secondary or args.profile):
         c5 = bench_c5(world, rank, 3, 3)
@@ -427,6 +466,8 @@ def run_single(args):
               "c3d128": ((8, 16, 16, 2048, 128), False, "bhsd"), "refshape": ((8, 12, 4, 4096, 64), True, "bhsd")}
     if args.workload in shapes:
         r = bench_prefill(*shapes[args.workload], flush, args.steps, args.warmup)
+    elif args.workload == "c4paged16":
+        r = bench_decode_paged(flush, args.steps, args.warmup, page_size=16)
     else:
         r = bench_decode(flush, args.steps, args.warmup, len_div=8 if args.workload == "c4small" else 1)
     print(json.dumps({"workload": args.workload, **r}), flush=True)
@@ -441,7 +482,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="short run for profiler captures: no secondary configs, no CPU baseline")
-    ap.add_argument("--workload", choices=["c2", "c3d64", "c3d128", "c4", "c4small", "refshape"], default=None,
+    ap.add_argument("--workload", choices=["c2", "c3d64", "c3d128", "c4", "c4small", "c4paged16", "refshape"],
+                    default=None,
                     help="profiler aid: run only this workload's kernel and print its timing")
     args = ap.parse_args()
     if args.workload:

@@ -28,6 +28,7 @@ constexpr int kStages = 3;
 constexpr int kConsumers = 4;     // warps
 constexpr int kThreads = 32 * (kConsumers + 1);
 constexpr int kMaxB = 4096;
+constexpr int kBtCacheEntries = 160;   // page indices cached per work item (chunk / page_size + 1)
 
 template <int D>
 struct DecCfg {
@@ -37,7 +38,8 @@ struct DecCfg {
   static constexpr int kAcc = kStages * kStage;            // fp32 [16][D] accumulator
   static constexpr int kRed = kAcc + 16 * D * 4;           // m, l [4][16] each
   static constexpr int kBar = kRed + 2 * kConsumers * 16 * 4;
-  static constexpr int kPrefix = kBar + 128;
+  static constexpr int kBtCache = kBar + 128;                // paged: page indices of one item
+  static constexpr int kPrefix = kBtCache + kBtCacheEntries * 4;
 };
 
 struct DecBars {
@@ -143,25 +145,40 @@ __global__ void __launch_bounds__(kThreads)
 
   if (warp == kConsumers) {
     // ------------------------------------------------------------ producer
+    // Lane 0 issues the TMA loads.  For a paged cache the whole warp first
+    // copies the item's page indices into shared memory (one coalesced load),
+    // so lane 0 never waits on the block table between loads.
+    int* bt_cache = reinterpret_cast<int*>(smem + C::kBtCache);
     if (lane == 0) {
       prefetch_tmap(&maps.k);
       prefetch_tmap(&maps.v);
-      uint32_t n = 0;
-      for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
-        const DecItem it = dec_item(p, prefix, idx);
-        const int len_b = p.kv_lens[it.b];
-        const int* bt_b = p.block_table ? p.block_table + (int64_t)it.b * p.max_pages : nullptr;
+    }
+    uint32_t n = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      const DecItem it = dec_item(p, prefix, idx);
+      const int len_b = p.kv_lens[it.b];
+      const int* bt_b = p.block_table ? p.block_table + (int64_t)it.b * p.max_pages : nullptr;
+      int pg0 = 0;
+      bool cached = false;
+      if (bt_b != nullptr) {
+        pg0 = (int)(it.t0 / p.page_size);
+        const int pg1 = (int)((it.t1 - 1) / p.page_size);
+        cached = pg1 - pg0 + 1 <= kBtCacheEntries;
+        if (cached)
+          for (int i = pg0 + lane; i <= pg1; i += 32) bt_cache[i - pg0] = bt_b[i];
+        __syncwarp();
+      }
+      if (lane == 0) {
         for (int64_t t = it.t0; t < it.t1; t += kTok, ++n) {
           const uint32_t s = n % kStages;
           if (!wc.wait(&bars.empty[s], ((n / kStages) & 1) ^ 1)) {
-            // unwinding: wait for the loads already in flight before exiting
-            for (uint32_t i = n > kStages ? n - kStages : 0; i < n; ++i)
-              drain_wait(&bars.full[i % kStages], (i / kStages) & 1, p.timeout_ns);
-            return;
+            ok = false;
+            break;
           }
           mbar_arrive_expect_tx(&bars.full[s], C::kStage);
           uint8_t* dst = smem + s * C::kStage;
-          if (p.block_table == nullptr) {
+          if (bt_b == nullptr) {
 #pragma unroll
             for (int pn = 0; pn < D / 64; ++pn) {
               tma_load_2d(dst + pn * C::kPanel, &maps.k, &bars.full[s], it.kvh * D + pn * 64, (int)t);
@@ -176,7 +193,8 @@ __global__ void __launch_bounds__(kThreads)
             for (int sub = 0; sub < kTok / bh; ++sub) {
               int tok = (int)t + sub * bh;
               if (tok > last) tok = last;
-              const int page = bt_b[tok / p.page_size];
+              const int pi = tok / p.page_size;
+              const int page = cached ? bt_cache[pi - pg0] : bt_b[pi];
               const int row = page * p.page_size + tok % p.page_size;
 #pragma unroll
               for (int pn = 0; pn < D / 64; ++pn) {
@@ -188,6 +206,14 @@ __global__ void __launch_bounds__(kThreads)
           }
         }
       }
+      __syncwarp();
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+    }
+    if (!ok && lane == 0) {
+      // unwinding: wait for the loads already in flight before exiting
+      for (uint32_t i = n > kStages ? n - kStages : 0; i < n; ++i)
+        drain_wait(&bars.full[i % kStages], (i / kStages) & 1, p.timeout_ns);
     }
     return;
   }
