@@ -37,6 +37,9 @@ SIGNATURES = {
     "bw_gqa_decode_static_scratch_bytes": (_sz, []),
     "bw_gqa_decode_static": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _f, _i, _vp]),
     "bw_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "bw_qk_norm_rope": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _f, _i, _vp, _vp]),
+    "bw_gqa_fused_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "bw_gqa_fused_fwd": (_i, [_vp] * 10 + [_i] * 8 + [_f, _i, _f, _i, _vp, _sz, _vp]),
     "bw_stream_status": (_i, [_vp]),
     "bw_set_option": (_i, [_i, _i64]),
     "bw_get_option": (_i64, [_i]),

@@ -232,3 +232,47 @@ def gqa_decode_paged(q, k_cache, v_cache, block_table, kv_lens, scale=None, chun
                                         workspace.numel() * workspace.element_size(), _stream())
     _ffi.check(rc, "bw_gqa_decode_paged")
     return o, lse
+
+
+def qk_norm_rope(x, cos_sin_cache, gamma=None, eps=1e-6, pos_offset=0, interleaved=False, out=None,
+                 return_rstd=False):
+    """QK-norm (RMSNorm over D, optional) + RoPE on a [B, H, S, D] bf16 tensor
+    (the prologue of the reference's fused op).  Returns y (and rstd fp32 [B, H, S])."""
+    if not x.is_cuda or x.dtype != torch.bfloat16 or x.stride(3) != 1:
+        raise ValueError("x must be a bf16 CUDA [B, H, S, D] tensor with contiguous D")
+    B, H, S, D = x.shape
+    y = out if out is not None else torch.empty((B, H, S, D), dtype=torch.bfloat16, device=x.device)
+    rstd = torch.empty((B, H, S), dtype=torch.float32, device=x.device) if return_rstd else None
+    xs = (ctypes.c_int64 * 3)(*_bhs(x))
+    ys = (ctypes.c_int64 * 3)(*_bhs(y))
+    cache = cos_sin_cache.contiguous()
+    g = gamma.contiguous() if gamma is not None else None
+    rc = _ffi.lib().bw_qk_norm_rope(_ptr(x), _ptr(y), B, H, S, D, xs, ys, _ptr(cache), cache.shape[0], int(pos_offset),
+                                    _ptr(g), float(eps), int(bool(interleaved)), _ptr(rstd), _stream())
+    _ffi.check(rc, "bw_qk_norm_rope")
+    return (y, rstd) if return_rstd else y
+
+
+def gqa_fused_fwd(q, k, v, cos_sin_cache, q_gamma=None, k_gamma=None, eps=1e-6, pos_offset=0, interleaved=False,
+                  scale=None, causal=False):
+    """QK-norm + RoPE + GQA attention (the reference's fused op), BHSD contiguous.
+    Returns (O, LSE, q_rstd, k_rstd)."""
+    B, Hq, Hkv, S, _, D = _check_inputs(q, k, v)
+    for t in (q, k, v):
+        if not t.is_contiguous():
+            raise ValueError("gqa_fused_fwd expects contiguous BHSD tensors")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    ws = torch.empty(int(_ffi.lib().bw_gqa_fused_workspace_size(B, Hq, Hkv, S, D)), dtype=torch.uint8,
+                     device=q.device)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, Hq, S), dtype=torch.float32, device=q.device)
+    qr = torch.empty((B, Hq, S), dtype=torch.float32, device=q.device)
+    kr = torch.empty((B, Hkv, S), dtype=torch.float32, device=q.device)
+    cache = cos_sin_cache.contiguous()
+    rc = _ffi.lib().bw_gqa_fused_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), _ptr(cache),
+                                     _ptr(q_gamma), _ptr(k_gamma), _ptr(qr), _ptr(kr), B, Hq, Hkv, S, Hq // Hkv, D,
+                                     cache.shape[0], int(pos_offset), float(eps), int(bool(interleaved)),
+                                     float(scale), int(bool(causal)), _ptr(ws), ws.numel(), _stream())
+    _ffi.check(rc, "bw_gqa_fused_fwd")
+    return o, lse, qr, kr

@@ -378,6 +378,63 @@ int bw_gqa_decode_paged(const void* Q, const void* K_cache, const void* V_cache,
   return bw::launch_lse_combine(c, s) == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
+int bw_qk_norm_rope(const void* X, void* Y, int B, int H, int S, int D, const int64_t* x_strides,
+                    const int64_t* y_strides, const float* cos_sin_cache, int cache_seq_len, int pos_offset,
+                    const float* gamma, float eps, int interleaved, float* rstd, void* stream) {
+  if (!X || !Y || !cos_sin_cache) return BW_ERR_NULL;
+  if (B <= 0 || H <= 0 || S <= 0 || (D != 64 && D != 128) || cache_seq_len < 0 || !(eps >= 0.f))
+    return BW_ERR_SHAPE;
+  int64_t xs[3], ys[3];
+  if (x_strides) { for (int i = 0; i < 3; ++i) xs[i] = x_strides[i]; } else { contiguous(H, S, D, xs); }
+  if (y_strides) { for (int i = 0; i < 3; ++i) ys[i] = y_strides[i]; } else { contiguous(H, S, D, ys); }
+  for (int i = 0; i < 3; ++i)
+    if (xs[i] <= 0 || ys[i] <= 0 || (xs[i] % 8) || (ys[i] % 8)) return BW_ERR_ALIGN;
+  if (!aligned16(X) || !aligned16(Y)) return BW_ERR_ALIGN;
+  DeviceState* dev = nullptr;
+  int rc = get_device_state(&dev);
+  if (rc != BW_OK) return rc;
+  bw::NormRopeParams p{};
+  p.in = X;
+  p.out = Y;
+  p.in_sb = xs[0]; p.in_sh = xs[1]; p.in_ss = xs[2];
+  p.out_sb = ys[0]; p.out_sh = ys[1]; p.out_ss = ys[2];
+  p.B = B; p.H = H; p.S = S; p.D = D;
+  p.cache = cos_sin_cache;
+  p.cache_seq_len = cache_seq_len;
+  p.pos_offset = pos_offset;
+  p.gamma = gamma;
+  p.eps = eps;
+  p.rstd = rstd;
+  p.neox = interleaved ? 0 : 1;
+  return bw::launch_norm_rope(p, dev->num_sms, static_cast<cudaStream_t>(stream)) == cudaSuccess ? BW_OK
+                                                                                                 : BW_ERR_CUDA;
+}
+
+size_t bw_gqa_fused_workspace_size(int B, int Hq, int Hkv, int S, int D) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || D <= 0) return 0;
+  return align256((size_t)B * Hq * S * D * 2) + align256((size_t)B * Hkv * S * D * 2);
+}
+
+int bw_gqa_fused_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, const float* cos_sin_cache,
+                     const float* q_gamma, const float* k_gamma, float* q_rstd, float* k_rstd, int B, int Hq,
+                     int Hkv, int S, int G, int D, int cache_seq_len, int pos_offset, float eps, int interleaved,
+                     float scale, int causal, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace) return BW_ERR_NULL;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0) return BW_ERR_SHAPE;
+  if (workspace_bytes < bw_gqa_fused_workspace_size(B, Hq, Hkv, S, D)) return BW_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return BW_ERR_ALIGN;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* q2 = ws;
+  void* k2 = ws + align256((size_t)B * Hq * S * D * 2);
+  int rc = bw_qk_norm_rope(Q, q2, B, Hq, S, D, nullptr, nullptr, cos_sin_cache, cache_seq_len, pos_offset, q_gamma,
+                           eps, interleaved, q_rstd, stream);
+  if (rc != BW_OK) return rc;
+  rc = bw_qk_norm_rope(K, k2, B, Hkv, S, D, nullptr, nullptr, cos_sin_cache, cache_seq_len, pos_offset, k_gamma,
+                       eps, interleaved, k_rstd, stream);
+  if (rc != BW_OK) return rc;
+  return attn_fwd(q2, k2, V, O, LSE, B, Hq, Hkv, S, S, G, D, scale, causal, nullptr, stream);
+}
+
 int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
                    float* LSE, void* stream) {
   if (!O_part || !LSE_part || !O) return BW_ERR_NULL;

@@ -74,6 +74,22 @@ struct CombineParams {
 
 cudaError_t launch_lse_combine(const CombineParams& p, cudaStream_t stream);
 
+// QK-norm + RoPE prologue over a [B, H, S, D] bf16 tensor (in place allowed).
+struct NormRopeParams {
+  const void* in;
+  void* out;
+  int64_t in_sb, in_sh, in_ss, out_sb, out_sh, out_ss;   // element strides
+  int B, H, S, D;
+  const float* cache;        // fp32 [cache_seq_len, D]: cos | sin
+  int cache_seq_len, pos_offset;
+  const float* gamma;        // fp32 [D] or null (no norm)
+  float eps;
+  float* rstd;               // fp32 [B, H, S] or null
+  int neox;                  // 1: pairs (i, i + D/2); 0: pairs (2i, 2i + 1)
+};
+
+cudaError_t launch_norm_rope(const NormRopeParams& p, int num_sms, cudaStream_t stream);
+
 // Per-device state owned by api.cu: the device error word, the SM count and the
 // driver's cuTensorMapEncodeTiled.  Returns a bw_attn status code.
 int device_context(int** err, int* num_sms, void** encode_fn);

@@ -151,6 +151,30 @@ BW_API int bw_gqa_decode_static(const void* Q, const void* K, const void* V, con
 BW_API int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
                    float* LSE, void* stream);
 
+/* QK-norm + RoPE prologue of the reference's fused op
+ * (src/SM103/attention/GQA_fused_sm103.cu:59-104; its ground truth :328-420),
+ * on a [B, H, S, D] bf16 tensor X -> Y (Y may equal X).  Per row:
+ *   rstd = 1/sqrt(mean(x^2) + eps); x = bf16(x * rstd * gamma)  (gamma NULL: skipped)
+ *   RoPE at p = s + pos_offset when 0 <= p < cache_seq_len, with the fp32
+ *   cos|sin cache [cache_seq_len, D]; interleaved = 0: NeoX pairs (i, i+D/2),
+ *   1: GPT-J pairs (2i, 2i+1).  rstd (fp32 [B, H, S]) may be NULL.
+ * x_strides / y_strides: element strides of (b, h, s), NULL = contiguous. */
+BW_API int bw_qk_norm_rope(const void* X, void* Y, int B, int H, int S, int D, const int64_t* x_strides,
+                           const int64_t* y_strides, const float* cos_sin_cache, int cache_seq_len, int pos_offset,
+                           const float* gamma, float eps, int interleaved, float* rstd, void* stream);
+
+/* QK-norm + RoPE + GQA attention: replaces launch_gqa_fused_v0<Br,Bc,D>(Q,K,V,O,LSE,
+ * cache, q_gamma, k_gamma, q_rstd, k_rstd, B,Hq,Hkv,G,S, cache_seq_len,
+ * pos_offset, eps, interleaved, scale, is_causal) (GQA_fused_sm103.cu:284-313),
+ * BHSD contiguous.  The normalised Q and K go to a caller workspace of
+ * bw_gqa_fused_workspace_size(B, Hq, Hkv, S, D) bytes; Q, K are not modified. */
+BW_API size_t bw_gqa_fused_workspace_size(int B, int Hq, int Hkv, int S, int D);
+BW_API int bw_gqa_fused_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE,
+                            const float* cos_sin_cache, const float* q_gamma, const float* k_gamma, float* q_rstd,
+                            float* k_rstd, int B, int Hq, int Hkv, int S, int G, int D, int cache_seq_len,
+                            int pos_offset, float eps, int interleaved, float scale, int causal, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Synchronise `stream`, then read and clear this device's error word.
  * Returns BW_OK, BW_ERR_TIMEOUT, BW_ERR_WORKSPACE or BW_ERR_CUDA. */
 BW_API int bw_stream_status(void* stream);

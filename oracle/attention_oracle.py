@@ -158,3 +158,52 @@ def sdpa_cpu(q, k, v, scale, causal=False):
     import torch.nn.functional as F
 
     return F.scaled_dot_product_attention(q, k, v, scale=scale, enable_gqa=True, is_causal=causal)
+
+
+def _bf16_round(x):
+    """Round float32 values to bfloat16 (nearest even) and widen back to float32."""
+    import torch
+
+    return torch.from_numpy(np.asarray(x, dtype=np.float32)).bfloat16().float().numpy()
+
+
+def norm_rope_reference(x, cache, gamma, eps, pos_offset, interleaved):
+    """QK-norm + RoPE of the reference's fused op, restated from
+    src/SM103/attention/GQA_fused_sm103.cu:59-104 (norm_rope_tile) with the same
+    rounding points: fp32 math, bf16 after the norm, bf16 after the rotation.
+    x: [B, H, S, D] (bf16 values as float32); cache: fp32 [L, D] (cos | sin).
+    Returns (y [B, H, S, D] float32 holding bf16 values, rstd [B, H, S] float32)."""
+    x = np.asarray(x, dtype=np.float32)
+    B, H, S, D = x.shape
+    half = D // 2
+    rstd = np.zeros((B, H, S), np.float32)
+    if gamma is not None:
+        ss = (x.astype(np.float32) ** 2).sum(-1, dtype=np.float32)
+        rstd = (1.0 / np.sqrt(ss / np.float32(D) + np.float32(eps))).astype(np.float32)
+        x = _bf16_round(x * rstd[..., None] * np.asarray(gamma, np.float32))
+    y = x.copy()
+    L = cache.shape[0]
+    for s in range(S):
+        pos = s + pos_offset
+        if not (0 <= pos < L):
+            continue
+        c = cache[pos, :half].astype(np.float32)
+        sn = cache[pos, half:].astype(np.float32)
+        if interleaved:
+            a, b = x[:, :, s, 0::2], x[:, :, s, 1::2]
+            y[:, :, s, 0::2] = a * c - b * sn
+            y[:, :, s, 1::2] = a * sn + b * c
+        else:
+            a, b = x[:, :, s, :half], x[:, :, s, half:]
+            y[:, :, s, :half] = a * c - b * sn
+            y[:, :, s, half:] = a * sn + b * c
+    return _bf16_round(y), rstd
+
+
+def rope_cache(max_pos, D, theta=10000.0):
+    """fp32 cos|sin cache [max_pos, D] in the reference's layout (cos in [0, D/2),
+    sin in [D/2, D)) with the standard inverse-frequency schedule theta^(-2i/D)."""
+    half = D // 2
+    inv = theta ** (-np.arange(half, dtype=np.float64) * 2.0 / D)
+    ang = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None]
+    return np.concatenate([np.cos(ang), np.sin(ang)], axis=1).astype(np.float32)

@@ -97,3 +97,11 @@ def test_shard_plan_partitions(units, world):
         assert b == c and a <= b
     sizes = [e - b for b, e in spans]
     assert max(sizes) - min(sizes) <= 1
+
+
+def test_package_exports():
+    import blackwell_b200 as bw
+    for name in ["gqa_fwd", "gqa_causal_fwd", "gqa_split_fwd", "mha_fwd", "gqa_decode", "gqa_decode_paged",
+                 "gqa_decode_partial", "lse_combine", "qk_norm_rope", "gqa_fused_fwd", "sdpa_gqa", "sdpa_gqa_causal",
+                 "stream_status", "set_option", "get_option", "shard_plan", "decode_workspace_size"]:
+        assert callable(getattr(bw, name)), name
