@@ -9,6 +9,9 @@
 // bw_attn status code (the reference returns void, so existing call sites that
 // ignore the result still compile).
 #pragma once
+#include <cstddef>
+#include <cstdio>
+
 #include <cuda_bf16.h>
 
 #include "bw_attn.h"
@@ -42,6 +45,25 @@ template <int Br, int Bc, int D>
 inline int launch_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, __nv_bfloat16* O,
                       float scale, int S, int B, int H) {
   return bw_mha_fwd(Q, K, V, O, nullptr, B, H, S, D, scale, nullptr, nullptr);
+}
+
+// Reads `n` float32 values from a headerless file written by the reference's
+// Python generators (base/baseline_gqa.py:165-170); the reference's own loadBin
+// (include/utils/kernelUtils.cuh:191-199) exits on error, this returns false.
+inline bool loadBin(const char* path, float* buf, size_t n) {
+  FILE* f = std::fopen(path, "rb");
+  if (!f) return false;
+  const size_t got = std::fread(buf, sizeof(float), n, f);
+  std::fclose(f);
+  return got == n;
+}
+
+// Writes `n` float32 values in the same headerless format.
+inline bool saveBin(const char* path, const float* buf, size_t n) {
+  FILE* f = std::fopen(path, "wb");
+  if (!f) return false;
+  const size_t put = std::fwrite(buf, sizeof(float), n, f);
+  return std::fclose(f) == 0 && put == n;
 }
 
 }  // namespace bw_compat
