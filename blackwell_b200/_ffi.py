@@ -12,7 +12,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libbw_attn.so"
 
 BW_OK, BW_ERR_SHAPE, BW_ERR_ALIGN, BW_ERR_CUDA, BW_ERR_TIMEOUT, BW_ERR_NCCL, BW_ERR_NULL, BW_ERR_WORKSPACE = range(8)
-BW_OPT_TIMEOUT_NS, BW_OPT_P_IN_TMEM, BW_OPT_DEBUG_FLAGS, BW_OPT_MAX_CTAS, BW_OPT_EXP_POLY = 1, 2, 3, 4, 5
+BW_OPT_TIMEOUT_NS, BW_OPT_P_IN_TMEM, BW_OPT_DEBUG_FLAGS, BW_OPT_MAX_CTAS, BW_OPT_EXP_POLY, BW_OPT_PREFILL_KERNEL = 1, 2, 3, 4, 5, 6
 
 # Every symbol the header declares, with (restype, argtypes).
 _vp, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t

@@ -34,6 +34,7 @@ std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
 std::atomic<int64_t> g_exp_poly{2};
+std::atomic<int64_t> g_prefill_kernel{1};
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -63,10 +64,11 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // 4-D map over a [B, H, S, D] bf16 tensor with element strides (sb, sh, ss, 1):
 // dims (D, S, H, B), box (64, 128, 1, 1), 128-byte swizzle, zero fill out of bounds.
-int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, const int64_t st[3]) {
+int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, const int64_t st[3],
+                  uint32_t box_rows = 128) {
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -122,10 +124,12 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   int rc = get_device_state(&dev);
   if (rc != BW_OK) return rc;
 
+  const bool v2 = g_prefill_kernel.load() == 2;
+  const uint32_t kv_rows = v2 ? 64u : 128u;
   bw::FmhaMaps maps;
   if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
-  if (make_map_bhsd(&maps.k, K, B, Hkv, Skv, D, st.k) != BW_OK) return BW_ERR_CUDA;
-  if (make_map_bhsd(&maps.v, V, B, Hkv, Skv, D, st.v) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_bhsd(&maps.k, K, B, Hkv, Skv, D, st.k, kv_rows) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_bhsd(&maps.v, V, B, Hkv, Skv, D, st.v, kv_rows) != BW_OK) return BW_ERR_CUDA;
 
   bw::FmhaParams p{};
   p.O = O;
@@ -152,7 +156,8 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   int ctas = dev->num_sms;
   const int64_t cap = g_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = (int)cap;
-  cudaError_t e = bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas, static_cast<cudaStream_t>(stream));
+  cudaError_t e = v2 ? bw::launch_fmha_fwd2(p, maps, (int)g_exp_poly.load(), ctas, static_cast<cudaStream_t>(stream))
+                     : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
@@ -487,6 +492,10 @@ int bw_set_option(int key, int64_t value) {
       if (value < 0) return BW_ERR_SHAPE;
       g_max_ctas = value;
       return BW_OK;
+    case BW_OPT_PREFILL_KERNEL:
+      if (value != 1 && value != 2) return BW_ERR_SHAPE;
+      g_prefill_kernel = value;
+      return BW_OK;
     case BW_OPT_EXP_POLY:
       if (value != 0 && value != 2 && value != 3 && value != 4) return BW_ERR_SHAPE;
       g_exp_poly = value;
@@ -502,6 +511,7 @@ int64_t bw_get_option(int key) {
     case BW_OPT_DEBUG_FLAGS: return g_debug_flags.load();
     case BW_OPT_MAX_CTAS: return g_max_ctas.load();
     case BW_OPT_EXP_POLY: return g_exp_poly.load();
+    case BW_OPT_PREFILL_KERNEL: return g_prefill_kernel.load();
     default: return -1;
   }
 }

@@ -24,13 +24,18 @@ struct FmhaParams {
 };
 
 struct FmhaMaps {
-  CUtensorMap q, k, v;           // 4-D (D, S, H, B) bf16, box (64, 128, 1, 1), SWIZZLE_128B
+  CUtensorMap q, k, v;           // 4-D (D, S, H, B) bf16, box (64, rows, 1, 1), SWIZZLE_128B;
+                                 // rows = 128 for Q; 128 (launch_fmha_fwd) or 64 (launch_fmha_fwd2) for K, V
 };
 
 // exp_poly: of every 8 pairs of exponentials, how many run as the FMA-pipe
 // polynomial instead of MUFU ex2 (0, 2, 3 or 4).
 cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int exp_poly, int num_sms,
                             cudaStream_t stream);
+
+// Double-buffered-S variant: 64-row K/V tiles (maps.k / maps.v with 64-row boxes).
+cudaError_t launch_fmha_fwd2(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
+                             cudaStream_t stream);
 
 // Split-KV single-token decode over ragged, contiguous per-sequence KV.
 struct DecodeParams {

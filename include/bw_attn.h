@@ -189,13 +189,20 @@ BW_API int bw_stream_status(void* stream);
  *   BW_OPT_MAX_CTAS        cap on the persistent prefill grid (0 = SM count)
  *   BW_OPT_EXP_POLY        of every 8 pairs of softmax exponentials, how many
  *                          are computed by an FMA-pipe polynomial instead of
- *                          MUFU ex2: 0, 2 (default), 3 or 4 */
+ *                          MUFU ex2: 0, 2 (default), 3 or 4
+ *   BW_OPT_PREFILL_KERNEL  1 (default): 128-key tiles, one score buffer per
+ *                          query block; 2: 64-key tiles, two score buffers per
+ *                          query block (QK^T of the next tile overlaps the
+ *                          softmax; slower on B200 because an N=64 QK^T MMA
+ *                          costs about as much as an N=128 one).
+ *                          BW_OPT_P_IN_TMEM applies to kernel 1 only. */
 enum {
   BW_OPT_TIMEOUT_NS = 1,
   BW_OPT_P_IN_TMEM = 2,
   BW_OPT_DEBUG_FLAGS = 3,
   BW_OPT_MAX_CTAS = 4,
-  BW_OPT_EXP_POLY = 5
+  BW_OPT_EXP_POLY = 5,
+  BW_OPT_PREFILL_KERNEL = 6
 };
 BW_API int bw_set_option(int key, int64_t value);
 BW_API int64_t bw_get_option(int key);

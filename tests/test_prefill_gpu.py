@@ -16,15 +16,19 @@ pytestmark = pytest.mark.gpu
 GOLDEN_GQA = ["gqa_nc_d128", "gqa_causal_d128", "gqa_causal_d64_g3_rand", "gqa_causal_d64_ragged", "gqa_split_d64"]
 
 
-@pytest.fixture(scope="module", params=[1, 0], ids=["p_tmem", "p_smem"])
+@pytest.fixture(scope="module", params=[(2, 1), (1, 1), (1, 0)], ids=["k2_dbuf", "k1_p_tmem", "k1_p_smem"])
 def p_variant(request):
-    """Kernel variants: P fed to the PV MMA from TMEM or from shared memory."""
+    """Kernel variants: 64-key tiles with two score buffers (kernel 2), or
+    128-key tiles with P fed to the PV MMA from TMEM or shared memory (kernel 1)."""
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
-    old = bw.get_option(_ffi.BW_OPT_P_IN_TMEM)
-    bw.set_option(_ffi.BW_OPT_P_IN_TMEM, request.param)
+    keys = (_ffi.BW_OPT_PREFILL_KERNEL, _ffi.BW_OPT_P_IN_TMEM)
+    old = [bw.get_option(k_) for k_ in keys]
+    for k_, v_ in zip(keys, request.param):
+        bw.set_option(k_, v_)
     yield request.param
-    bw.set_option(_ffi.BW_OPT_P_IN_TMEM, old)
+    for k_, v_ in zip(keys, old):
+        bw.set_option(k_, v_)
 
 
 def _run(q, k, v, scale, causal):
