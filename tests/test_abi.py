@@ -103,5 +103,6 @@ def test_package_exports():
     import blackwell_b200 as bw
     for name in ["gqa_fwd", "gqa_causal_fwd", "gqa_split_fwd", "mha_fwd", "gqa_decode", "gqa_decode_paged",
                  "gqa_decode_partial", "lse_combine", "qk_norm_rope", "gqa_fused_fwd", "sdpa_gqa", "sdpa_gqa_causal",
-                 "stream_status", "set_option", "get_option", "shard_plan", "decode_workspace_size"]:
+                 "stream_status", "set_option", "get_option", "shard_plan", "decode_workspace_size",
+                 "attention_from_host"]:
         assert callable(getattr(bw, name)), name
