@@ -29,6 +29,8 @@ SIGNATURES = {
     "bw_gqa_causal_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _SP, _vp]),
     "bw_gqa_split_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _i, _SP, _vp]),
     "bw_mha_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _SP, _vp]),
+    "bw_mha_f32_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "bw_mha_fwd_f32": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _SP, _vp, _sz, _vp]),
     "bw_gqa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i64, _i]),
     "bw_gqa_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _f, _i, _vp, _sz, _vp]),
     "bw_gqa_decode_paged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _sz,

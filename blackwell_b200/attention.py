@@ -337,3 +337,25 @@ def attention_from_host(q_host, k_host, v_host, o_host, lse_host=None, scale=Non
     cur.wait_stream(s_out)
     cur.wait_stream(s_cmp)
     return o_host, lse_host
+
+
+def mha_fwd_f32(q, k, v, scale=None, out=None, lse=None):
+    """fp32 MHA forward (the reference's mha_v3_tc data types: fp32 in / out), D = 64;
+    Q K^T on TF32 tensor cores, P V in bf16 (V rounded to bf16 in a workspace):
+    q, k, v [B, H, S, 64] float32 CUDA views with contiguous D.  Returns (O fp32, LSE)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda or t.dtype != torch.float32 or t.dim() != 4 or t.stride(3) != 1:
+            raise ValueError(f"{name} must be a float32 CUDA [B, H, S, D] tensor with contiguous D")
+    B, H, S, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must have the same shape")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o = out if out is not None else torch.empty((B, H, S, D), dtype=torch.float32, device=q.device)
+    if lse is None:
+        lse = torch.empty((B, H, S), dtype=torch.float32, device=q.device)
+    ws = torch.empty(int(_ffi.lib().bw_mha_f32_workspace_size(B, H, S, D)), dtype=torch.uint8, device=q.device)
+    rc = _ffi.lib().bw_mha_fwd_f32(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, S, D, float(scale),
+                                   _strides(q, k, v, o), _ptr(ws), ws.numel(), _stream())
+    _ffi.check(rc, "bw_mha_fwd_f32")
+    return o, lse

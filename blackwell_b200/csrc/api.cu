@@ -65,12 +65,14 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // 4-D map over a [B, H, S, D] bf16 tensor with element strides (sb, sh, ss, 1):
 // dims (D, S, H, B), box (64, 128, 1, 1), 128-byte swizzle, zero fill out of bounds.
 int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, const int64_t st[3],
-                  uint32_t box_rows = 128) {
+                  uint32_t box_rows = 128, bool fp32 = false) {
+  const uint32_t eb = fp32 ? 4 : 2;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
-  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * eb, (cuuint64_t)st[1] * eb, (cuuint64_t)st[0] * eb};
+  cuuint32_t box[4] = {128 / eb, box_rows, 1, 1};   // 128-byte rows (the swizzle span)
   cuuint32_t es[4] = {1, 1, 1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+  CUresult r = g_encode(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                        const_cast<void*>(base), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
@@ -204,6 +206,71 @@ int bw_gqa_split_fwd(const void* Q, const void* K, const void* V, void* O, float
 int bw_mha_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int H, int S, int D,
                float scale, const bw_strides* strides, void* stream) {
   return attn_fwd(Q, K, V, O, LSE, B, H, H, S, S, 1, D, scale, 0, strides, stream);
+}
+
+size_t bw_mha_f32_workspace_size(int B, int H, int S, int D) {
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
+  return (size_t)B * H * S * D * 2;
+}
+
+int bw_mha_fwd_f32(const float* Q, const float* K, const float* V, float* O, float* LSE, int B, int H, int S, int D,
+                   float scale, const bw_strides* strides, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!Q || !K || !V || !O || !workspace) return BW_ERR_NULL;
+  if (workspace_bytes < bw_mha_f32_workspace_size(B, H, S, D)) return BW_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return BW_ERR_ALIGN;
+  if (B <= 0 || H <= 0 || S <= 0 || D != 64) return BW_ERR_SHAPE;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return BW_ERR_SHAPE;
+  if ((int64_t)B * H * ((S + 255) / 256) >= (int64_t(1) << 30)) return BW_ERR_SHAPE;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return BW_ERR_ALIGN;
+  bw_strides st;
+  if (strides) {
+    st = *strides;
+  } else {
+    contiguous(H, S, D, st.q);
+    contiguous(H, S, D, st.k);
+    contiguous(H, S, D, st.v);
+    contiguous(H, S, D, st.o);
+  }
+  for (const int64_t* a : {st.q, st.k, st.v, st.o})
+    for (int i = 0; i < 3; ++i)
+      if (a[i] <= 0 || (a[i] % 4) != 0) return BW_ERR_ALIGN;
+  DeviceState* dev = nullptr;
+  int rc = get_device_state(&dev);
+  if (rc != BW_OK) return rc;
+  bw::FmhaMaps maps;
+  if (make_map_bhsd(&maps.q, Q, B, H, S, D, st.q, 128, true) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_bhsd(&maps.k, K, B, H, S, D, st.k, 128, true) != BW_OK) return BW_ERR_CUDA;
+  // V -> bf16 (contiguous BHSD) in the workspace; the PV MMA runs on bf16 P and V
+  if (bw::launch_f32_to_bf16(V, st.v[0], st.v[1], st.v[2], workspace, B, H, S, D, dev->num_sms,
+                             static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return BW_ERR_CUDA;
+  int64_t vst[3];
+  contiguous(H, S, D, vst);
+  if (make_map_bhsd(&maps.v, workspace, B, H, S, D, vst, 128, false) != BW_OK) return BW_ERR_CUDA;
+  bw::FmhaParams p{};
+  p.O = O;
+  p.o_sb = st.o[0];
+  p.o_sh = st.o[1];
+  p.o_ss = st.o[2];
+  p.LSE = LSE;
+  p.B = B;
+  p.Hq = H;
+  p.Hkv = H;
+  p.G = 1;
+  p.Sq = S;
+  p.Skv = S;
+  p.D = D;
+  p.causal = 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.n_qtiles = (S + 127) / 128;
+  p.n_kvtiles = (S + 127) / 128;
+  p.pair_heads = 0;
+  p.num_items = B * H * ((p.n_qtiles + 1) / 2);
+  p.err = dev->err;
+  p.timeout_ns = (uint64_t)g_timeout_ns.load();
+  p.debug_flags = 0;
+  cudaError_t e = bw::launch_fmha_fwd_f32(p, maps, dev->num_sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
 size_t bw_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int64_t total_tokens, int chunk) {

@@ -33,6 +33,15 @@ struct FmhaMaps {
 cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int exp_poly, int num_sms,
                             cudaStream_t stream);
 
+// fp32 Q, K and output: QK^T with kind::tf32 MMAs; P (bf16 in TMEM) times V
+// (bf16, converted beforehand) with kind::f16; D = 64.  maps.q / maps.k are
+// FLOAT32 with 32-element, 128-row boxes, maps.v bf16 as usual; O is fp32.
+cudaError_t launch_fmha_fwd_f32(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream);
+
+// fp32 -> bf16 copy of a [B, H, S, D] tensor (contiguous destination).
+cudaError_t launch_f32_to_bf16(const float* src, int64_t sb, int64_t sh, int64_t ss, void* dst, int B, int H, int S,
+                               int D, int num_sms, cudaStream_t stream);
+
 // Double-buffered-S variant: 64-row K/V tiles (maps.k / maps.v with 64-row boxes).
 cudaError_t launch_fmha_fwd2(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream);

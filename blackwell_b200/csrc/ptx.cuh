@@ -195,6 +195,17 @@ __device__ __forceinline__ void mma_ts_lh(uint32_t d_tmem, uint32_t a_tmem, uint
       "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accum)
       : "memory");
 }
+// kind::tf32 form (fp32 operands in shared memory, read as TF32).
+__device__ __forceinline__ void mma_ss_lh_tf32(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                               uint32_t b_hi, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accum)
+      : "memory");
+}
 // Halves of sdesc_sw128(saddr, lbo, 1024).
 __device__ __forceinline__ uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo) {
   return ((saddr & 0x3FFFFu) >> 4) | ((lbo >> 4) << 16);
@@ -206,6 +217,11 @@ __host__ __device__ constexpr uint32_t sdesc_hi_sbo1024() { return (1024u >> 4) 
 // bit 24.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// kind::tf32: A and B format TF32 (= 2), D fp32.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N, bool b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 

@@ -86,6 +86,17 @@ BW_API int bw_gqa_split_fwd(const void* Q, const void* K, const void* V, void* O
 BW_API int bw_mha_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int H, int S, int D,
                float scale, const bw_strides* strides, void* stream);
 
+/* MHA forward with fp32 inputs and output, the data types of the reference's
+ * mha_v3_tc (src/SM120/attention/MHA_sm120.cu:64-71, fp32 via a 3-way TF32
+ * split).  Here Q K^T runs as kind::tf32 MMAs (10-bit mantissa inputs, fp32
+ * accumulation: logits to ~1e-3 relative) and P V as bf16 MMAs on V rounded to
+ * bf16 in `workspace` (bw_mha_f32_workspace_size bytes); O is fp32; D = 64; LSE
+ * optional.  Strides are fp32 element strides (multiples of 4). */
+BW_API size_t bw_mha_f32_workspace_size(int B, int H, int S, int D);
+BW_API int bw_mha_fwd_f32(const float* Q, const float* K, const float* V, float* O, float* LSE, int B, int H, int S,
+                          int D, float scale, const bw_strides* strides, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 /* Split-KV single-token decode.  No counterpart kernel exists in the reference;
  * the semantics are its split-length GQA (adhitya_GQA.cu:63-188) with Sq = 1
  * and Skv = kv_lens[b] per sequence.

@@ -203,3 +203,28 @@ def test_attention_from_host_pipelined(chunks):
     assert bw.stream_status() == 0
     ro, rl = bw.gqa_causal_fwd(q.cuda().transpose(1, 2), k.cuda().transpose(1, 2), v.cuda().transpose(1, 2))
     assert torch.equal(o.transpose(1, 2), ro.cpu()) and torch.equal(lse, rl.cpu())
+
+
+def test_mha_fp32_golden(golden):
+    """fp32 MHA (the reference's mha_v3_tc data types) against the reference's
+    fp64 ground truth on its own input distribution (U[0,1) - 0.5, fp32)."""
+    import blackwell_b200 as bw
+    g = golden("mha_fp32_d64")
+    q, k, v = (torch.from_numpy(g[n]).cuda() for n in ("q_f32", "k_f32", "v_f32"))
+    o, lse = bw.mha_fwd_f32(q, k, v, float(g["scale"]))
+    assert bw.stream_status() == 0
+    err = np.abs(o.cpu().numpy() - g["o_fp64"]).max()
+    assert err <= 2e-3, err      # TF32 logits, bf16 P and V
+
+
+@pytest.mark.parametrize("S", [1, 100, 384])
+def test_mha_fp32_shapes(S):
+    import blackwell_b200 as bw
+    B, H, D = 2, 3, 64
+    g = torch.Generator().manual_seed(S)
+    q, k, v = (torch.randn(B, H, S, D, generator=g) for _ in range(3))
+    o, lse = bw.mha_fwd_f32(q.cuda(), k.cuda(), v.cuda())
+    assert bw.stream_status() == 0
+    ro, rl = orc.fp64_reference(q, k, v, 1 / math.sqrt(D))
+    assert np.abs(o.cpu().numpy() - ro).max() <= O_TOL
+    assert np.abs(lse.cpu().numpy() - rl).max() <= 5e-3  # TF32 logits
