@@ -357,43 +357,45 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
       }
       const float msub = (m_run == -INFINITY) ? 0.f : m_run;
       const f2 cc2{c, c}, nm2{-msub, -msub};
-      // Phase 1: exponent arguments in place (independent paired FMAs).
+      // Argument, exponential (POLY of every 8 pairs on the FMA pipe, the rest on
+      // MUFU) and row sum per pair in one pass, so the scheduler can overlap the
+      // FMA/ALU work with the MUFU stream.
+      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
 #pragma unroll
       for (int k = 0; k < 64; ++k) {
         const f2 x = ffma2(f2{s[2 * k], s[2 * k + 1]}, cc2, nm2);
-        s[2 * k] = x.x;
-        s[2 * k + 1] = x.y;
-      }
-      // Phase 2: exponentials in place; POLY of every 8 pairs on the FMA pipe.
-#pragma unroll
-      for (int k = 0; k < 64; ++k) {
+        f2 e;
         if ((k & 7) < POLY) {
-          const f2 e = ex2_poly2(f2{s[2 * k], s[2 * k + 1]});
-          s[2 * k] = e.x;
-          s[2 * k + 1] = e.y;
+          e = ex2_poly2(x);
         } else {
-          s[2 * k] = ex2_mufu(s[2 * k]);
-          s[2 * k + 1] = ex2_mufu(s[2 * k + 1]);
+          e.x = ex2_mufu(x.x);
+          e.y = ex2_mufu(x.y);
         }
-      }
-      // Phase 3: row sum (four paired accumulators) and bf16 packing.
-      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
+        s[2 * k] = e.x;
+        s[2 * k + 1] = e.y;
+        if constexpr (PT) {
+          // first half of P (key columns 0..63 -> TMEM columns 0..31) goes out
+          // while the second half is still being exponentiated
+          if (k == 31) {
+            uint32_t pk0[32];
 #pragma unroll
-      for (int k = 0; k < 64; k += 4) {
-        acc0 = fadd2(acc0, f2{s[2 * k], s[2 * k + 1]});
-        acc1 = fadd2(acc1, f2{s[2 * k + 2], s[2 * k + 3]});
-        acc2 = fadd2(acc2, f2{s[2 * k + 4], s[2 * k + 5]});
-        acc3 = fadd2(acc3, f2{s[2 * k + 6], s[2 * k + 7]});
+            for (int i = 0; i < 32; ++i) pk0[i] = pack_bf16(s[2 * i], s[2 * i + 1]);
+            tmem_st32(s_tmem, pk0);
+          }
+        }
+        if ((k & 3) == 0) acc0 = fadd2(acc0, e);
+        else if ((k & 3) == 1) acc1 = fadd2(acc1, e);
+        else if ((k & 3) == 2) acc2 = fadd2(acc2, e);
+        else acc3 = fadd2(acc3, e);
       }
       acc0 = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
       l_run = l_run * corr + (acc0.x + acc0.y);
       BW_TRACE_AT(t == 0, 30 + w, sc - 1);
       if constexpr (PT) {
-        uint32_t pk[64];
+        uint32_t pk[32];
 #pragma unroll
-        for (int k = 0; k < 64; ++k) pk[k] = pack_bf16(s[2 * k], s[2 * k + 1]);
-        tmem_st32(s_tmem, pk);
-        tmem_st32(s_tmem + 32, pk + 32);
+        for (int k = 0; k < 32; ++k) pk[k] = pack_bf16(s[64 + 2 * k], s[64 + 2 * k + 1]);
+        tmem_st32(s_tmem + 32, pk);
       } else {
         uint32_t pk[64];
 #pragma unroll
