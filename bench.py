@@ -318,6 +318,28 @@ def bench_prefill(shape, causal, layout, flush, steps, warmup):
     return {"ms": t, "TFLOP/s": flops / t / 1e9}
 
 
+def bench_fused(shape, flush, steps, warmup):
+    """The reference's fused op (QK-norm + RoPE + causal GQA) at a prefill shape:
+    K's prologue as its own pass, Q's inside the attention kernel."""
+    import blackwell_b200 as bw
+    B, Hq, Hkv, S, D = shape
+    g = torch.Generator(device="cuda").manual_seed(42)
+    q = torch.randn(B, Hq, S, D, generator=g, device="cuda").bfloat16()
+    k = torch.randn(B, Hkv, S, D, generator=g, device="cuda").bfloat16()
+    v = torch.randn(B, Hkv, S, D, generator=g, device="cuda").bfloat16()
+    half = D // 2
+    inv = 10000.0 ** (-torch.arange(half, dtype=torch.float64, device="cuda") * 2.0 / D)
+    ang = torch.arange(S, dtype=torch.float64, device="cuda")[:, None] * inv[None]
+    cache = torch.cat([ang.cos(), ang.sin()], 1).float().contiguous()
+    qg = 1 + 0.1 * torch.randn(D, generator=g, device="cuda")
+    kg = 1 + 0.1 * torch.randn(D, generator=g, device="cuda")
+    fn = lambda: bw.gqa_fused_fwd(q, k, v, cache, qg, kg, causal=True)
+    ms = time_steps(fn, steps, warmup, flush, 1)
+    assert bw.stream_status() == 0
+    t = statistics.median(ms)
+    return {"ms": t, "TFLOP/s": causal_flops(B, Hq, S, D) / t / 1e9}
+
+
 def bench_c5(world, rank, steps, warmup):
     """C5: causal GQA B=1, Hq=64, Hkv=8, S=131072, D=128, one or more KV-head groups
     per rank (8 groups sharded over the ranks, no exchange).  Each rank holds only
@@ -412,7 +434,9 @@ def run_ours(args, world, rank, local):
         ref_shape = bench_prefill((8, 12, 4, 4096, 64), True, "bhsd", flush, sec_steps, 3)
         ref_shape["reference_V46_B300_ms"] = 0.5863
         secondary["reference_shape_causal_B8_Hq12_Hkv4_S4096_D64"] = ref_shape
-        for key in ("C3_mha_D64", "C3_mha_D128", "reference_shape_causal_B8_Hq12_Hkv4_S4096_D64"):
+        secondary["fused_norm_rope_causal_C2_bhsd"] = bench_fused((4, 32, 8, 4096, 128), flush, sec_steps, 3)
+        for key in ("C3_mha_D64", "C3_mha_D128", "reference_shape_causal_B8_Hq12_Hkv4_S4096_D64",
+                    "fused_norm_rope_causal_C2_bhsd"):
             secondary[key]["frac_of_peak"] = secondary[key]["TFLOP/s"] / peaks["bf16_tflops"]
         dec = bench_decode(flush, sec_steps, 3)
         dec["frac_of_hbm_peak"] = dec["GB/s"] / peaks["hbm_gbs"]

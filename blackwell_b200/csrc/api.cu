@@ -159,7 +159,8 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   const int64_t cap = g_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = (int)cap;
   cudaError_t e = v2 ? bw::launch_fmha_fwd2(p, maps, (int)g_exp_poly.load(), ctas, static_cast<cudaStream_t>(stream))
-                     : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas, static_cast<cudaStream_t>(stream));
+                     : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas,
+                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
@@ -456,12 +457,13 @@ int bw_qk_norm_rope(const void* X, void* Y, int B, int H, int S, int D, const in
   if (!X || !Y || !cos_sin_cache) return BW_ERR_NULL;
   if (B <= 0 || H <= 0 || S <= 0 || (D != 64 && D != 128) || cache_seq_len < 0 || !(eps >= 0.f))
     return BW_ERR_SHAPE;
+  if ((int64_t)B * H * S >= (int64_t(1) << 31)) return BW_ERR_SHAPE;
   int64_t xs[3], ys[3];
   if (x_strides) { for (int i = 0; i < 3; ++i) xs[i] = x_strides[i]; } else { contiguous(H, S, D, xs); }
   if (y_strides) { for (int i = 0; i < 3; ++i) ys[i] = y_strides[i]; } else { contiguous(H, S, D, ys); }
   for (int i = 0; i < 3; ++i)
     if (xs[i] <= 0 || ys[i] <= 0 || (xs[i] % 8) || (ys[i] % 8)) return BW_ERR_ALIGN;
-  if (!aligned16(X) || !aligned16(Y)) return BW_ERR_ALIGN;
+  if (!aligned16(X) || !aligned16(Y) || !aligned16(cos_sin_cache)) return BW_ERR_ALIGN;
   DeviceState* dev = nullptr;
   int rc = get_device_state(&dev);
   if (rc != BW_OK) return rc;
@@ -495,6 +497,10 @@ int bw_gqa_fused_fwd(const void* Q, const void* K, const void* V, void* O, float
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0) return BW_ERR_SHAPE;
   if (workspace_bytes < bw_gqa_fused_workspace_size(B, Hq, Hkv, S, D)) return BW_ERR_WORKSPACE;
   if (!aligned16(workspace)) return BW_ERR_ALIGN;
+  if (!cos_sin_cache) return BW_ERR_NULL;
+  if (cache_seq_len < 0 || !(eps >= 0.f)) return BW_ERR_SHAPE;
+  // Q and K are normalised and rotated into the workspace by the HBM-bound
+  // prologue kernel (one pass each), then read by the attention kernel.
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   void* q2 = ws;
   void* k2 = ws + align256((size_t)B * Hq * S * D * 2);

@@ -169,7 +169,8 @@ BW_API int bw_lse_combine(const float* O_part, const float* LSE_part, int splits
  *   RoPE at p = s + pos_offset when 0 <= p < cache_seq_len, with the fp32
  *   cos|sin cache [cache_seq_len, D]; interleaved = 0: NeoX pairs (i, i+D/2),
  *   1: GPT-J pairs (2i, 2i+1).  rstd (fp32 [B, H, S]) may be NULL.
- * x_strides / y_strides: element strides of (b, h, s), NULL = contiguous. */
+ * x_strides / y_strides: element strides of (b, h, s), NULL = contiguous.
+ * X, Y and the cache must be 16-byte aligned (BW_ERR_ALIGN otherwise). */
 BW_API int bw_qk_norm_rope(const void* X, void* Y, int B, int H, int S, int D, const int64_t* x_strides,
                            const int64_t* y_strides, const float* cos_sin_cache, int cache_seq_len, int pos_offset,
                            const float* gamma, float eps, int interleaved, float* rstd, void* stream);

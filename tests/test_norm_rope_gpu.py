@@ -38,21 +38,41 @@ def test_norm_rope(D, interleaved, with_norm):
         np.testing.assert_allclose(rstd.cpu().numpy(), rr, rtol=1e-5)
 
 
-def test_fused_attention():
+@pytest.mark.parametrize("D,Hq,Hkv,S,interleaved,with_norm,causal,pos_offset,cache_len", [
+    (128, 4, 2, 300, False, True, True, 0, 300),      # G even: two heads per work item
+    (128, 6, 2, 333, True, True, False, 5, 200),      # G odd: two query tiles per item; partly unrotated
+    (64, 8, 1, 257, False, False, True, -7, 400),     # RoPE only, negative offset
+    (64, 3, 3, 129, True, True, True, 0, 129),        # MHA
+])
+def test_fused_attention(D, Hq, Hkv, S, interleaved, with_norm, causal, pos_offset, cache_len):
+    """Q's prologue runs inside the attention kernel on each shared-memory tile,
+    K's as a separate pass; both against the restated reference math."""
     import blackwell_b200 as bw
-    B, Hq, Hkv, S, D = 1, 4, 2, 300, 128
+    B = 2
     q, k, v = seeded_bf16((B, Hq, S, D), 51), seeded_bf16((B, Hkv, S, D), 52), seeded_bf16((B, Hkv, S, D), 53)
-    cache = orc.rope_cache(S, D)
+    cache = orc.rope_cache(cache_len, D)
     g = torch.Generator().manual_seed(3)
-    qg = (1 + 0.1 * torch.randn(D, generator=g)).float()
-    kg = (1 + 0.1 * torch.randn(D, generator=g)).float()
-    o, lse, qr, kr = bw.gqa_fused_fwd(q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(cache).cuda(), qg.cuda(),
-                                      kg.cuda(), causal=True)
+    qg = (1 + 0.1 * torch.randn(D, generator=g)).float() if with_norm else None
+    kg = (1 + 0.1 * torch.randn(D, generator=g)).float() if with_norm else None
+    cu = lambda t: t.cuda() if t is not None else None
+    o, lse, qr, kr = bw.gqa_fused_fwd(q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(cache).cuda(), cu(qg), cu(kg),
+                                      pos_offset=pos_offset, interleaved=interleaved, causal=causal)
     assert bw.stream_status() == 0
-    q2, rq = orc.norm_rope_reference(q.float().numpy(), cache, qg.numpy(), 1e-6, 0, False)
-    k2, rk = orc.norm_rope_reference(k.float().numpy(), cache, kg.numpy(), 1e-6, 0, False)
-    ro, rl = orc.fp64_reference(q2, k2, v.float(), 1 / math.sqrt(D), causal=True)
+    npg = lambda t: t.numpy() if t is not None else None
+    q2, rq = orc.norm_rope_reference(q.float().numpy(), cache, npg(qg), 1e-6, pos_offset, interleaved)
+    k2, rk = orc.norm_rope_reference(k.float().numpy(), cache, npg(kg), 1e-6, pos_offset, interleaved)
+    ro, rl = orc.fp64_reference(q2, k2, v.float(), 1 / math.sqrt(D), causal=causal)
     assert np.abs(o.float().cpu().numpy() - ro).max() <= O_TOL
     assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL
-    np.testing.assert_allclose(qr.cpu().numpy(), rq, rtol=1e-5)
-    np.testing.assert_allclose(kr.cpu().numpy(), rk, rtol=1e-5)
+    if with_norm:
+        np.testing.assert_allclose(qr.cpu().numpy(), rq, rtol=1e-5)
+        np.testing.assert_allclose(kr.cpu().numpy(), rk, rtol=1e-5)
+    # the fused Q prologue and the standalone one give the same attention
+    q3 = bw.qk_norm_rope(q.cuda(), torch.from_numpy(cache).cuda(), cu(qg), pos_offset=pos_offset,
+                         interleaved=interleaved)
+    k3 = bw.qk_norm_rope(k.cuda(), torch.from_numpy(cache).cuda(), cu(kg), pos_offset=pos_offset,
+                         interleaved=interleaved)
+    fn = bw.gqa_causal_fwd if causal else bw.gqa_fwd
+    o3, lse3 = fn(q3, k3, v.cuda())
+    assert (o3.float() - o.float()).abs().max().item() <= 2 ** -7
+    assert (lse3 - lse).abs().max().item() <= 5e-4
