@@ -34,7 +34,7 @@ std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
 std::atomic<int64_t> g_exp_poly{2};
-std::atomic<int64_t> g_prefill_kernel{1};
+std::atomic<int64_t> g_prefill_kernel{0};   // 0: by head dimension (3 for D = 128, 1 for D = 64)
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -126,7 +126,9 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   int rc = get_device_state(&dev);
   if (rc != BW_OK) return rc;
 
-  const bool v2 = g_prefill_kernel.load() == 2;
+  int kern = (int)g_prefill_kernel.load();
+  if (kern == 0) kern = D == 128 ? 3 : 1;
+  const bool v2 = kern == 2;
   const uint32_t kv_rows = v2 ? 64u : 128u;
   bw::FmhaMaps maps;
   if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
@@ -152,15 +154,17 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   p.n_kvtiles = (Skv + 127) / 128;
   p.pair_heads = (G % 2 == 0) ? 1 : 0;
   p.num_items = p.pair_heads ? B * (Hq / 2) * p.n_qtiles : B * Hq * ((p.n_qtiles + 1) / 2);
+  if (kern == 3) p.num_items = B * Hq * (causal ? (p.n_qtiles + 1) / 2 : p.n_qtiles);
   p.err = dev->err;
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.debug_flags = (int)g_debug_flags.load();
   int ctas = dev->num_sms;
   const int64_t cap = g_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = (int)cap;
-  cudaError_t e = v2 ? bw::launch_fmha_fwd2(p, maps, (int)g_exp_poly.load(), ctas, static_cast<cudaStream_t>(stream))
-                     : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas,
-                                          static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = kern == 3 ? bw::launch_fmha_fwd3(p, maps, (int)g_exp_poly.load(), ctas, s)
+                  : v2      ? bw::launch_fmha_fwd2(p, maps, (int)g_exp_poly.load(), ctas, s)
+                            : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas, s);
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
@@ -566,7 +570,7 @@ int bw_set_option(int key, int64_t value) {
       g_max_ctas = value;
       return BW_OK;
     case BW_OPT_PREFILL_KERNEL:
-      if (value != 1 && value != 2) return BW_ERR_SHAPE;
+      if (value < 0 || value > 3) return BW_ERR_SHAPE;
       g_prefill_kernel = value;
       return BW_OK;
     case BW_OPT_EXP_POLY:

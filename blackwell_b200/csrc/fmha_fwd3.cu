@@ -1,0 +1,530 @@
+// GQA / MHA flash-attention forward for sm_100a, one query tile per work item
+// with double-buffered scores.
+//
+// Same operator as fmha_fwd.cu (per query row i of head hq, KV head hq / G:
+// O[i] = softmax(scale * Q[i] K^T) V, LSE[i] = ln sum_j exp(scale * Q[i].K[j]),
+// optional causal mask j <= i), the behaviour of the reference's
+// launch_gqa_vN / gqa_causal launchers (src/SM103/attention/GQA_sm103.cu:5733-6516,
+// GQA_sm103_causal_v3.cu:2156-2180) and the split-length launcher
+// (src/SM120/attention/adhitya_GQA.cu:199-213).
+//
+// Design (one persistent CTA per SM, 11 warps):
+//   warps 0-7  softmax: one 128-row query tile; row r is shared by thread r
+//              of warps 0-3 (keys 0-63 of every key tile, "half 0") and
+//              thread r of warps 4-7 (keys 64-127, "half 1")
+//   warp  8    TMA producer: the Q tile, then K and V tiles in MMA order
+//   warp  9    PV MMA issuer (one thread) and TMEM owner
+//   warp 10    QK^T MMA issuer (one thread)
+// The two halves of a row run independent online softmaxes (own running max
+// and sum) into their own accumulators O_0 = sum over half-0 keys of p V and
+// O_1 likewise, and are merged once per row at the end:
+//   m = max(m_0, m_1), w_h = 2^(m_h - m), L = l_0 w_0 + l_1 w_1,
+//   O = (O_0 w_0 + O_1 w_1) / L,  LSE = ln 2 (m + log2 L).
+// Tensor memory: S0 | S1 (128 fp32 columns each) | O_0 | O_1 (D columns each).
+// Key tile j of an item uses score buffer (t + j) % 2, t counting the tiles
+// of all earlier items; half h writes its P (bf16) over columns
+// [64 h, 64 h + 32) of that buffer.  MMA order per item of n key tiles:
+//   QK(0), QK(1), then for each j: PV(j), QK(j + 2)
+// so while the softmax works on tile j the tensor core runs PV(j - 1) and
+// QK(j + 1) is already waiting in the other buffer: the softmax of one tile
+// overlaps the MMAs of its neighbours instead of waiting for them, and the two
+// threads per row give each SM sub-partition two softmax warps to interleave.
+// (The two-query-block design of fmha_fwd.cu cannot double-buffer: two blocks
+// x (2 score buffers + O) needs 768 columns of the 512.)
+//
+// Online softmax in the log2 domain with the FlashAttention-4 lazy rescale
+// (running max raised only when a tile's max exceeds it by more than 8), as
+// in fmha_fwd.cu, per half.  A rescale of O_h at tile j first waits for PV(j - 1).
+#include "kernels.h"
+#include "ptx.cuh"
+#include "softmax_math.cuh"
+#include "tmem_io.cuh"
+
+namespace bw {
+namespace {
+
+constexpr int kRows = 128;
+constexpr int kSmemBudget = 232448 - 2048;
+constexpr int kMaxSlots = 12;
+
+template <int D>
+struct L3 {
+  static constexpr int kTile = kRows * D * 2;   // one 128-row bf16 tile
+  static constexpr int kSub = kRows * 128;      // one 128-byte swizzle panel
+  static constexpr int kPanels = D / 64;
+  static constexpr int kQ = 0;
+  static constexpr int kKV = kTile;
+  static constexpr int kNSraw = (kSmemBudget - kKV - 512 - 2 * kRows * 8) / kTile;
+  static constexpr int NS = kNSraw > kMaxSlots ? kMaxSlots : kNSraw;
+  static constexpr int kBar = kKV + NS * kTile;
+  static constexpr int kX = kBar + 512;                   // (m, l) exchange: [2 halves][128 rows] float2
+  static constexpr int kBytes = kX + 2 * kRows * 8;
+  static_assert(NS >= 4, "K/V ring needs at least 4 slots");
+};
+
+struct Bars3 {
+  uint64_t q_full, q_empty, s_full[2], p_full[2], pv_done[2], o_full, o_empty, mma_done, qk_done, xch;
+  uint64_t kv_full[kMaxSlots], kv_empty[kMaxSlots];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// A work item is one (b, hq) head and one query tile (non-causal) or the
+// pair of query tiles (nqt - 1 - p, p) (causal: nqt + 1 key tiles in total
+// whatever p, so items weigh the same).  Items are numbered head-major, so the
+// CTAs running at any moment work on a few neighbouring heads and the K / V
+// tiles they share stay in L2 (query-tile-major order made 148 concurrent CTAs
+// stream 148 different heads and re-read K / V from DRAM about six times).
+struct Item3 {
+  int b, h, kvh, nseg;
+  int qt[2], n[2];
+};
+
+__device__ __forceinline__ Item3 decode_item3(const FmhaParams& p, int idx) {
+  Item3 it;
+  const int per_head = p.causal ? (p.n_qtiles + 1) >> 1 : p.n_qtiles;
+  const int r = idx / per_head;
+  const int u = idx - r * per_head;
+  it.b = r / p.Hq;
+  it.h = r - it.b * p.Hq;
+  it.kvh = it.h / p.G;
+  if (p.causal) {
+    it.qt[0] = p.n_qtiles - 1 - u;
+    it.qt[1] = u;
+    it.nseg = it.qt[1] == it.qt[0] ? 1 : 2;
+    it.n[0] = min(it.qt[0] + 1, p.n_kvtiles);
+    it.n[1] = min(it.qt[1] + 1, p.n_kvtiles);
+  } else {
+    it.qt[0] = it.qt[1] = u;
+    it.nseg = 1;
+    it.n[0] = it.n[1] = p.n_kvtiles;
+  }
+  return it;
+}
+
+// ------------------------------------------------------------ producer warp
+// Loads, per item, the Q tile and then the K / V tiles in the order the MMA
+// thread consumes them: K0, K1, then V(j), K(j + 2) for j = 0 .. n - 1.
+template <int D>
+__device__ void producer3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc) {
+  using L = L3<D>;
+  constexpr int NS = L::NS;
+  uint32_t ld = 0, qn = 0;
+  uint32_t armed = 0;
+  bool ok = true;
+  bool first_k = true;
+  auto load_kv = [&](bool is_k, int tile, const Item3& it) -> bool {
+    const uint32_t slot = ld % NS;
+    if (!wc.wait(&bars.kv_empty[slot], ((ld / NS) & 1) ^ 1)) return false;
+    const bool withhold = is_k && first_k && (p.debug_flags & 1);
+    if (is_k) first_k = false;
+    if (!withhold) {
+      mbar_arrive_expect_tx(&bars.kv_full[slot], L::kTile);
+      uint8_t* dst = smem + L::kKV + slot * L::kTile;
+      const CUtensorMap* m = is_k ? &maps.k : &maps.v;
+      for (int c = 0; c < L::kPanels; ++c)
+        tma_load_4d(dst + c * L::kSub, m, &bars.kv_full[slot], c * 64, tile * kRows, it.kvh, it.b);
+      armed |= 1u << slot;
+    } else {
+      armed &= ~(1u << slot);
+    }
+    ++ld;
+    return true;
+  };
+  for (int idx = blockIdx.x; ok && idx < p.num_items; idx += gridDim.x) {
+    const Item3 it = decode_item3(p, idx);
+    for (int sg = 0; ok && sg < it.nseg; ++sg) {
+      const int n = sg == 0 ? it.n[0] : it.n[1];
+      if (!wc.wait(&bars.q_empty, (qn & 1) ^ 1)) { ok = false; break; }
+      mbar_arrive_expect_tx(&bars.q_full, L::kTile);
+      for (int c = 0; c < L::kPanels; ++c)
+        tma_load_4d(smem + L::kQ + c * L::kSub, &maps.q, &bars.q_full, c * 64, (sg == 0 ? it.qt[0] : it.qt[1]) * kRows, it.h, it.b);
+      ++qn;
+      ok = load_kv(true, 0, it);
+      if (ok && n > 1) ok = load_kv(true, 1, it);
+      for (int j = 0; ok && j < n; ++j) {
+        ok = load_kv(false, j, it);
+        if (ok && j + 2 < n) ok = load_kv(true, j + 2, it);
+      }
+    }
+  }
+  if (!ok) {
+    for (uint32_t i = (ld > NS ? ld - NS : 0); i < ld; ++i) {
+      const uint32_t slot = i % NS;
+      if (armed & (1u << slot)) drain_wait(&bars.kv_full[slot], (i / NS) & 1, wc.timeout_ns);
+    }
+    if (qn) drain_wait(&bars.q_full, (qn - 1) & 1, wc.timeout_ns);
+  }
+}
+
+// ---------------------------------------------------------------- MMA warps
+// Two issuing threads, one per MMA kind, so that one thread's barrier waits
+// overlap the other's issue (an issuing thread blocks while the tensor pipe
+// drains its queue, ~70 cycles per 128x128x16 MMA; a single issuer waiting for
+// P, K and V in series left the pipe idle for about a third of every tile).
+//   QK issuer: QK(g) into score buffer g % 2 for the global tile index g, once
+//              PV(g - 2) (which reads P(g - 2) from that buffer) has completed.
+//   PV issuer: PV(g) once the softmax has written P(g).
+// Ring positions of an item's K / V tiles (the producer's order): K0 at 0,
+// K1 at 1, then V(j) and K(j + 2) alternate; with e0 the item's first position
+// and n >= 2: K(j) at e0 + (j < 2 ? j : 2j - 1); V(j) at e0 + 2 + 2j for
+// j <= n - 2 and e0 + 2n - 1 for j = n - 1; with n = 1: K0 at e0, V0 at e0 + 1.
+// The issuers poll without suspending (a suspended thread wakes a few hundred
+// cycles after the phase completes); measured equal to suspending waits, which
+// would matter only if the polling took issue slots from the softmax warps.
+__device__ __forceinline__ bool issuer_wait(const WaitCtl& wc, uint64_t* bar, uint32_t parity) {
+  return spin_wait(wc, bar, parity);
+}
+__device__ __forceinline__ uint32_t pos_k(int j) { return j < 2 ? (uint32_t)j : (uint32_t)(2 * j - 1); }
+__device__ __forceinline__ uint32_t pos_v(int j, int n) {
+  if (n == 1) return 1;
+  return j <= n - 2 ? (uint32_t)(2 + 2 * j) : (uint32_t)(2 * n - 1);
+}
+
+template <int D>
+__device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
+  using L = L3<D>;
+  constexpr int NS = L::NS;
+  constexpr int SUB = L::kSub;
+  constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 128, false);
+  constexpr uint32_t HI = sdesc_hi_sbo1024();
+  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t q_lo = sdesc_lo(smem_base + L::kQ, 16);
+  const uint32_t k_lo0 = sdesc_lo(smem_base + L::kKV, 16);
+  uint32_t e0 = 0, qn = 0, tc = 0;
+  bool ok = true;
+  for (int idx = blockIdx.x; ok && idx < p.num_items; idx += gridDim.x) {
+    const Item3 it = decode_item3(p, idx);
+    for (int sg = 0; ok && sg < it.nseg; ++sg) {
+      const int n = sg == 0 ? it.n[0] : it.n[1];
+      if (!wc.wait(&bars.q_full, qn & 1)) { ok = false; break; }
+      ++qn;
+      for (int j = 0; j < n; ++j) {
+        const uint32_t g = tc + j, buf = g & 1;
+        const uint32_t e = e0 + pos_k(j);
+        if (!wc.wait(&bars.kv_full[e % NS], (e / NS) & 1)) { ok = false; break; }
+        if (g >= 2 && !issuer_wait(wc, &bars.pv_done[buf], ((g - 2) >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ka = k_lo0 + (e % NS) * (uint32_t)(L::kTile / 16);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t off = ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
+          mma_ss_lh(tmem + buf * 128, q_lo + off, HI, ka + off, HI, IDESC_QK, ks > 0);
+        }
+        tc_commit(&bars.s_full[buf]);
+        tc_commit(&bars.kv_empty[e % NS]);
+        if (j == n - 1) tc_commit(&bars.q_empty);
+      }
+      if (!ok) break;
+      tc += n;
+      e0 += 2 * n;
+    }
+  }
+  tc_commit(&bars.qk_done);
+  drain_wait(&bars.qk_done, 0, wc.timeout_ns);
+}
+
+template <int D>
+__device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
+  using L = L3<D>;
+  constexpr int NS = L::NS;
+  constexpr int SUB = L::kSub;
+  constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, true);
+  constexpr uint32_t HI = sdesc_hi_sbo1024();
+  const uint32_t v_lo0 = sdesc_lo(smem_u32(smem) + L::kKV, SUB);   // V operand (MN-major)
+  uint32_t e0 = 0, tc = 0, itn = 0;
+  bool ok = true;
+  for (int idx = blockIdx.x; ok && idx < p.num_items; idx += gridDim.x) {
+    const Item3 it = decode_item3(p, idx);
+    for (int sg = 0; ok && sg < it.nseg; ++sg) {
+      const int n = sg == 0 ? it.n[0] : it.n[1];
+      for (int j = 0; j < n; ++j) {
+        const uint32_t g = tc + j, buf = g & 1;
+        const uint32_t e = e0 + pos_v(j, n);
+        if (!wc.wait(&bars.kv_full[e % NS], (e / NS) & 1)) { ok = false; break; }
+        // the previous tile's epilogue must have read O before PV(0) overwrites it
+        if (j == 0 && itn > 0 && !wc.wait(&bars.o_empty, (itn - 1) & 1)) { ok = false; break; }
+        if (!issuer_wait(wc, &bars.p_full[buf], (g >> 1) & 1)) { ok = false; break; }
+        BW_TRACE_AT(true, 6, g);
+        tc_fence_after();
+        const uint32_t va = v_lo0 + (e % NS) * (uint32_t)(L::kTile / 16);
+        // half h: O_h += P_h (TMEM columns 64 h .. 64 h + 31 of the buffer) * V rows 64 h .. 64 h + 63
+#pragma unroll
+        for (int ks = 0; ks < kRows / 16; ++ks) {
+          const int h = ks >> 2;
+          mma_ts_lh(tmem + 256 + h * D, tmem + buf * 128 + h * 64 + (ks & 3) * 8, va + (ks * 16 * 128) / 16, HI,
+                    IDESC_PV, ((ks & 3) > 0 || j > 0) ? 1u : 0u);
+        }
+        BW_TRACE_AT(true, 8, g);
+        tc_commit(&bars.pv_done[buf]);
+        tc_commit(&bars.kv_empty[e % NS]);
+      }
+      if (!ok) break;
+      tc_commit(&bars.o_full);
+      tc += n;
+      e0 += 2 * n;
+      ++itn;
+    }
+  }
+  tc_commit(&bars.mma_done);
+  drain_wait(&bars.mma_done, 0, wc.timeout_ns);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// ----------------------------------------------------------- softmax warps
+// Thread t (0..255): row t % 128 of the item's tile (TMEM lane), half t / 128.
+template <int D, int POLY>
+__device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
+  using L = L3<D>;
+  const int rl = t & 127, half = t >> 7;
+  const uint32_t lane_off = (uint32_t)((rl >> 5) * 32) << 16;
+  const uint32_t o_own = tmem + lane_off + 256 + half * D;
+  const float c = p.scale_log2;
+  float2* xch = reinterpret_cast<float2*>(smem + L::kX);
+  uint32_t tc = 0, itn = 0;
+
+  for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
+    const Item3 it = decode_item3(p, idx);
+    for (int sg = 0; sg < it.nseg; ++sg) {
+    const int n = sg == 0 ? it.n[0] : it.n[1];
+    const int qt = sg == 0 ? it.qt[0] : it.qt[1];
+    const int row = qt * kRows + rl;
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const uint32_t g = tc + j, buf = g & 1;
+      const uint32_t s_tmem = tmem + lane_off + buf * 128 + half * 64;
+      if (!wc.wait(&bars.s_full[buf], (g >> 1) & 1)) return;
+      BW_TRACE_AT(t == 0, 0, g);
+      BW_TRACE_AT(t == 128, 4, g);
+      tc_fence_after();
+      uint32_t r[64];
+      tmem_ld64(s_tmem, r);
+      BW_TRACE_AT(t == 0, 1, g);
+      float* s = reinterpret_cast<float*>(r);
+      const int kv0 = j * kRows + half * 64;
+      if ((p.causal && kv0 + 63 > qt * kRows) || kv0 + 64 > p.Skv) {
+        int lim = p.Skv - kv0;
+        if (p.causal) lim = min(lim, row + 1 - kv0);
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i >= lim) s[i] = -INFINITY;
+      }
+      float mx;
+      {
+        float a[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a[u] = fmaxf(s[u], s[8 + u]);
+#pragma unroll
+        for (int i = 16; i < 64; i += 16)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
+        mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+      }
+      const float m_cand = mx * c;
+      float corr = 1.f;
+      const bool upd = m_cand > m_run + 8.f;
+      if (upd) {
+        corr = ex2_mufu(m_run - m_cand);
+        m_run = m_cand;
+      }
+      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
+      const f2 cc2{c, c}, nm2{-msub, -msub};
+      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const f2 x = ffma2(f2{s[2 * k], s[2 * k + 1]}, cc2, nm2);
+        f2 e;
+        if ((k & 7) < POLY) {
+          e = ex2_poly2(x);
+        } else {
+          e.x = ex2_mufu(x.x);
+          e.y = ex2_mufu(x.y);
+        }
+        s[2 * k] = e.x;
+        s[2 * k + 1] = e.y;
+        if ((k & 3) == 0) acc0 = fadd2(acc0, e);
+        else if ((k & 3) == 1) acc1 = fadd2(acc1, e);
+        else if ((k & 3) == 2) acc2 = fadd2(acc2, e);
+        else acc3 = fadd2(acc3, e);
+      }
+      acc0 = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
+      l_run = l_run * corr + (acc0.x + acc0.y);
+      BW_TRACE_AT(t == 0, 2, g);
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) pk[k] = pack_bf16_3(s[2 * k], s[2 * k + 1]);
+        tmem_st32(s_tmem, pk);
+      }
+      if (j > 0 && __any_sync(0xffffffffu, upd)) {
+        // O_h must hold PV(j - 1) before it is rescaled
+        if (!wc.wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1)) return;
+        tc_fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(o_own + c0, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+          tmem_st32(o_own + c0, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars.p_full[buf]);
+      BW_TRACE_AT(t == 0, 3, g);
+      BW_TRACE_AT(t == 128, 5, g);
+      BW_TRACE_AT((t & 31) == 0 && t < 128, 10 + (t >> 5), g);
+      BW_TRACE_AT((t & 31) == 0 && t >= 128, 14 + ((t - 128) >> 5), g);
+    }
+    // merge the two halves of the row: exchange (m, l) through shared memory
+    xch[half * kRows + rl] = make_float2(m_run, l_run);
+    mbar_arrive(&bars.xch);
+    if (!wc.wait(&bars.xch, itn & 1)) return;
+    const float2 other = xch[(half ^ 1) * kRows + rl];
+    const float m0 = half == 0 ? m_run : other.x, l0 = half == 0 ? l_run : other.y;
+    const float m1 = half == 0 ? other.x : m_run, l1 = half == 0 ? other.y : l_run;
+    const float m = fmaxf(m0, m1);
+    const float w0 = m0 == -INFINITY ? 0.f : ex2_mufu(m0 - m);
+    const float w1 = m1 == -INFINITY ? 0.f : ex2_mufu(m1 - m);
+    const float lsum = l0 * w0 + l1 * w1;
+    const float inv_l = 1.f / lsum;
+    const float a0 = w0 * inv_l, a1 = w1 * inv_l;
+    if (!wc.wait(&bars.o_full, itn & 1)) return;
+    tc_fence_after();
+    // this thread writes output columns [half * D/2, half * D/2 + D/2)
+    const uint32_t o0 = tmem + lane_off + 256 + half * (D / 2);
+    uint32_t q[D / 4];
+#pragma unroll
+    for (int c0 = 0; c0 < D / 2; c0 += 32) {
+      uint32_t x0[32], x1[32];
+      tmem_ld32(o0 + c0, x0);
+      tmem_ld32(o0 + D + c0, x1);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        q[c0 / 2 + i] = pack_bf16_3(__uint_as_float(x0[2 * i]) * a0 + __uint_as_float(x1[2 * i]) * a1,
+                                    __uint_as_float(x0[2 * i + 1]) * a0 + __uint_as_float(x1[2 * i + 1]) * a1);
+    }
+    // O has been read: the next item's first PV may overwrite it
+    tc_fence_before();
+    mbar_arrive(&bars.o_empty);
+    if (row < p.Sq) {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.O) + it.b * p.o_sb + it.h * p.o_sh +
+                                            (int64_t)row * p.o_ss + half * (D / 2));
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) dst[i] = make_uint4(q[4 * i], q[4 * i + 1], q[4 * i + 2], q[4 * i + 3]);
+      if (p.LSE != nullptr && half == 0)
+        p.LSE[((int64_t)it.b * p.Hq + it.h) * p.Sq + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
+    }
+    tc += n;
+    ++itn;
+    }
+  }
+}
+
+constexpr int kThreads3 = 352;
+
+template <int D, int POLY>
+__global__ void __launch_bounds__(kThreads3, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
+  using L = L3<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars3& bars = *reinterpret_cast<Bars3*>(smem + L::kBar);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  if (tid == 0) {
+    mbar_init(&bars.q_full, 1);
+    mbar_init(&bars.q_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars.s_full[b], 1);
+      mbar_init(&bars.p_full[b], 256);
+    }
+    mbar_init(&bars.pv_done[0], 1);
+    mbar_init(&bars.pv_done[1], 1);
+    mbar_init(&bars.qk_done, 1);
+    mbar_init(&bars.o_full, 1);
+    mbar_init(&bars.o_empty, 256);
+    mbar_init(&bars.xch, 256);
+    mbar_init(&bars.mma_done, 1);
+    for (int s = 0; s < L::NS; ++s) {
+      mbar_init(&bars.kv_full[s], 1);
+      mbar_init(&bars.kv_empty[s], 1);
+    }
+    bars.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8 && lane == 0) {
+    prefetch_tmap(&maps.q);
+    prefetch_tmap(&maps.k);
+    prefetch_tmap(&maps.v);
+  }
+  if (warp == 9) tmem_alloc(&bars.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_base;
+  WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, warp};
+
+  if (warp < 8) {
+    softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
+  } else if (warp == 8) {
+    if (lane == 0) producer3<D>(p, maps, smem, bars, wc);
+  } else {
+    if (lane == 0) {
+      if (warp == 9) pv_issuer3<D>(p, smem, bars, wc, tmem);
+      else qk_issuer3<D>(p, smem, bars, wc, tmem);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D, int POLY>
+cudaError_t launch3(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
+  constexpr int bytes = L3<D>::kBytes + 1024;
+  auto kern = fmha_fwd3_kernel<D, POLY>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  const int grid = p.num_items < num_sms ? p.num_items : num_sms;
+  kern<<<grid, kThreads3, bytes, stream>>>(p, maps);
+  return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t launch3_poly(const FmhaParams& p, const FmhaMaps& maps, int poly, int num_sms, cudaStream_t stream) {
+  switch (poly) {
+    case 0: return launch3<D, 0>(p, maps, num_sms, stream);
+    case 2: return launch3<D, 2>(p, maps, num_sms, stream);
+    case 3: return launch3<D, 3>(p, maps, num_sms, stream);
+    case 4: return launch3<D, 4>(p, maps, num_sms, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
+                             cudaStream_t stream) {
+  if (p.D == 128) return launch3_poly<128>(p, maps, exp_poly, num_sms, stream);
+  if (p.D == 64) return launch3_poly<64>(p, maps, exp_poly, num_sms, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace bw
+
+#ifdef BW_TRACE
+extern "C" __attribute__((visibility("default"))) int bw_trace_read3(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, g_bw_trace, sizeof(g_bw_trace));
+  return 64 * 512;
+}
+#endif

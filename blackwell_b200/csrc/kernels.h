@@ -46,6 +46,10 @@ cudaError_t launch_f32_to_bf16(const float* src, int64_t sb, int64_t sh, int64_t
 cudaError_t launch_fmha_fwd2(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream);
 
+// One query tile per work item, double-buffered scores (one softmax warpgroup).
+cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
+                             cudaStream_t stream);
+
 // Split-KV single-token decode over ragged, contiguous per-sequence KV.
 struct DecodeParams {
   const void* Q;                 // bf16 [B, Hq, D], strides q_sb, q_sh

@@ -103,6 +103,25 @@ struct WaitCtl {
   }
 };
 
+// Same contract as WaitCtl::wait, polling with test_wait (the thread never
+// suspends): a thread that must react within tens of cycles, such as the MMA
+// issuer waiting for P, uses this.
+__device__ __forceinline__ bool spin_wait(const WaitCtl& wc, uint64_t* bar, uint32_t parity) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_test(bar, parity)) return true;
+    if (*wc.abort_flag) return false;
+    if (globaltimer_ns() - t0 > wc.timeout_ns) {
+      *wc.abort_flag = 1;
+      atomicCAS(wc.err, 0, 0x100 | wc.site);
+      return false;
+    }
+  }
+}
+
 // Bounded wait used while unwinding after an abort: ignores the abort flag so
 // that copies and MMAs already in flight are waited for before TMEM and shared
 // memory are released.

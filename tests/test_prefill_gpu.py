@@ -16,10 +16,13 @@ pytestmark = pytest.mark.gpu
 GOLDEN_GQA = ["gqa_nc_d128", "gqa_causal_d128", "gqa_causal_d64_g3_rand", "gqa_causal_d64_ragged", "gqa_split_d64"]
 
 
-@pytest.fixture(scope="module", params=[(2, 1), (1, 1), (1, 0)], ids=["k2_dbuf", "k1_p_tmem", "k1_p_smem"])
+@pytest.fixture(scope="module", params=[(3, 1), (2, 1), (1, 1), (1, 0)],
+                ids=["k3_split_rows", "k2_dbuf", "k1_p_tmem", "k1_p_smem"])
 def p_variant(request):
-    """Kernel variants: 64-key tiles with two score buffers (kernel 2), or
-    128-key tiles with P fed to the PV MMA from TMEM or shared memory (kernel 1)."""
+    """Kernel variants: one query block with two score buffers and rows split
+    over two threads (kernel 3), 64-key tiles with two score buffers
+    (kernel 2), or two query blocks with P fed to the PV MMA from TMEM or
+    shared memory (kernel 1)."""
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
     keys = (_ffi.BW_OPT_PREFILL_KERNEL, _ffi.BW_OPT_P_IN_TMEM)
