@@ -93,9 +93,16 @@ __device__ __forceinline__ Item decode_item(const FmhaParams& p, int idx) {
   } else {
     const int ntp = (p.n_qtiles + 1) >> 1;
     const int per_t = p.B * p.Hq;
-    int tp = idx / per_t;
-    const int r = idx - tp * per_t;
-    if (p.causal) tp = ntp - 1 - tp;
+    int tp, r;
+    if (p.causal) {
+      tp = idx / per_t;
+      r = idx - tp * per_t;
+      tp = ntp - 1 - tp;  // heaviest query tiles first
+    } else {
+      // head-major: the CTAs running at once share a few heads' K / V in L2
+      r = idx / ntp;
+      tp = idx - r * ntp;
+    }
     it.b = r / p.Hq;
     it.head[0] = it.head[1] = r - it.b * p.Hq;
     t0 = 2 * tp;
