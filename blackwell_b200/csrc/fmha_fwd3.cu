@@ -8,33 +8,34 @@
 // GQA_sm103_causal_v3.cu:2156-2180) and the split-length launcher
 // (src/SM120/attention/adhitya_GQA.cu:199-213).
 //
-// Design (one persistent CTA per SM, 11 warps):
-//   warps 0-7  softmax: one 128-row query tile; row r is shared by thread r
-//              of warps 0-3 (keys 0-63 of every key tile, "half 0") and
-//              thread r of warps 4-7 (keys 64-127, "half 1")
-//   warp  8    TMA producer: the Q tile, then K and V tiles in MMA order
-//   warp  9    PV MMA issuer (one thread) and TMEM owner
-//   warp 10    QK^T MMA issuer (one thread)
-// The two halves of a row run independent online softmaxes (own running max
-// and sum) into their own accumulators O_0 = sum over half-0 keys of p V and
-// O_1 likewise, and are merged once per row at the end:
-//   m = max(m_0, m_1), w_h = 2^(m_h - m), L = l_0 w_0 + l_1 w_1,
-//   O = (O_0 w_0 + O_1 w_1) / L,  LSE = ln 2 (m + log2 L).
-// Tensor memory: S0 | S1 (128 fp32 columns each) | O_0 | O_1 (D columns each).
-// Key tile j of an item uses score buffer (t + j) % 2, t counting the tiles
-// of all earlier items; half h writes its P (bf16) over columns
-// [64 h, 64 h + 32) of that buffer.  MMA order per item of n key tiles:
-//   QK(0), QK(1), then for each j: PV(j), QK(j + 2)
+// Design (one persistent CTA per SM, 4 N + 3 warps, N = 2):
+//   warps 0 .. 4N-1  softmax: one 128-row query tile; row r is shared by
+//                    thread r of warps 4q .. 4q+3 for q = 0 .. N-1 ("part" q
+//                    takes keys qK .. qK+K-1 of every key tile, K = 128 / N)
+//   warp 4N          TMA producer: the Q tile, then K and V tiles in MMA order
+//   warp 4N+1        PV MMA issuer (one thread) and TMEM owner
+//   warp 4N+2        QK^T MMA issuer (one thread)
+// The parts of a row run independent online softmaxes (own running max and
+// sum) into their own accumulators O_q = sum over part-q keys of p V, and are
+// merged once per row at the end:
+//   m = max_q m_q, w_q = 2^(m_q - m), L = sum_q l_q w_q,
+//   O = sum_q O_q w_q / L,  LSE = ln 2 (m + log2 L).
+// Tensor memory: S_0 .. S_{NB-1} (128 fp32 columns each; NB = 2 at D = 128,
+// 3 at D = 64) | O_0 .. O_{N-1} (D columns each).  Global key tile g (counted
+// over all items of the CTA) uses score buffer g % NB; part q writes its P
+// (bf16) over columns [qK, qK + K/2) of that buffer.  MMA order per item of n
+// key tiles:
+//   QK(0), QK(1), then for each j: PV(j), QK(j + 2)   (two issuing threads below)
 // so while the softmax works on tile j the tensor core runs PV(j - 1) and
-// QK(j + 1) is already waiting in the other buffer: the softmax of one tile
-// overlaps the MMAs of its neighbours instead of waiting for them, and the two
-// threads per row give each SM sub-partition two softmax warps to interleave.
+// QK(j + 1) is already waiting in another buffer: the softmax of one tile
+// overlaps the MMAs of its neighbours instead of waiting for them, and the N
+// threads per row give each SM sub-partition N softmax warps to interleave.
 // (The two-query-block design of fmha_fwd.cu cannot double-buffer: two blocks
 // x (2 score buffers + O) needs 768 columns of the 512.)
 //
 // Online softmax in the log2 domain with the FlashAttention-4 lazy rescale
 // (running max raised only when a tile's max exceeds it by more than 8), as
-// in fmha_fwd.cu, per half.  A rescale of O_h at tile j first waits for PV(j - 1).
+// in fmha_fwd.cu, per part.  A rescale of O_q at tile j first waits for PV(j - 1).
 #include "kernels.h"
 #include "ptx.cuh"
 #include "softmax_math.cuh"
@@ -47,6 +48,22 @@ constexpr int kRows = 128;
 constexpr int kSmemBudget = 232448 - 2048;
 constexpr int kMaxSlots = 12;
 
+// N threads per query row, each taking kKeys = 128 / N keys of every key tile
+// into its own accumulator O_part (D columns), and NB score buffers of 128
+// columns: TMEM holds S_0 .. S_{NB-1} | O_0 .. O_{N-1}, NB 128 + N D <= 512.
+// D = 128: N = 2, NB = 2.  D = 64: N = 2, NB = 3 (the third buffer lets
+// QK(g + 1) start before PV(g - 1) has finished; N = 4 with two buffers
+// measured slower, the PV -> QK chain bounding it).
+template <int D>
+struct Split {
+  static constexpr int N = 2;
+  static constexpr int NB = D == 128 ? 2 : 3;
+  static constexpr int kKeys = 128 / N;
+  static constexpr int kOCol = NB * 128;          // first TMEM column of O_0
+  static constexpr int kThreads = 128 * N + 96;   // + producer, PV issuer, QK issuer warps
+  static_assert(NB * 128 + N * D <= 512, "TMEM: score buffers and accumulators");
+};
+
 template <int D>
 struct L3 {
   static constexpr int kTile = kRows * D * 2;   // one 128-row bf16 tile
@@ -54,16 +71,17 @@ struct L3 {
   static constexpr int kPanels = D / 64;
   static constexpr int kQ = 0;
   static constexpr int kKV = kTile;
-  static constexpr int kNSraw = (kSmemBudget - kKV - 512 - 2 * kRows * 8) / kTile;
+  static constexpr int kXBytes = Split<D>::N * kRows * 8;     // (m, l) exchange: [N parts][128 rows] float2
+  static constexpr int kNSraw = (kSmemBudget - kKV - 512 - kXBytes) / kTile;
   static constexpr int NS = kNSraw > kMaxSlots ? kMaxSlots : kNSraw;
   static constexpr int kBar = kKV + NS * kTile;
-  static constexpr int kX = kBar + 512;                   // (m, l) exchange: [2 halves][128 rows] float2
-  static constexpr int kBytes = kX + 2 * kRows * 8;
+  static constexpr int kX = kBar + 512;
+  static constexpr int kBytes = kX + kXBytes;
   static_assert(NS >= 4, "K/V ring needs at least 4 slots");
 };
 
 struct Bars3 {
-  uint64_t q_full, q_empty, s_full[2], p_full[2], pv_done[2], o_full, o_empty, mma_done, qk_done, xch;
+  uint64_t q_full, q_empty, s_full[3], p_full[3], pv_done[3], o_full, o_empty, mma_done, qk_done, xch;
   uint64_t kv_full[kMaxSlots], kv_empty[kMaxSlots];
   uint32_t tmem_base;
   int abort_flag;
@@ -200,10 +218,13 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
       if (!wc.wait(&bars.q_full, qn & 1)) { ok = false; break; }
       ++qn;
       for (int j = 0; j < n; ++j) {
-        const uint32_t g = tc + j, buf = g & 1;
+        constexpr uint32_t NB = Split<D>::NB;
+        const uint32_t g = tc + j, buf = g % NB;
         const uint32_t e = e0 + pos_k(j);
         if (!wc.wait(&bars.kv_full[e % NS], (e / NS) & 1)) { ok = false; break; }
-        if (g >= 2 && !issuer_wait(wc, &bars.pv_done[buf], ((g - 2) >> 1) & 1)) { ok = false; break; }
+        BW_TRACE_AT(true, 22, g);
+        if (g >= NB && !issuer_wait(wc, &bars.pv_done[buf], ((g - NB) / NB) & 1)) { ok = false; break; }
+        BW_TRACE_AT(true, 23, g);
         tc_fence_after();
         const uint32_t ka = k_lo0 + (e % NS) * (uint32_t)(L::kTile / 16);
 #pragma unroll
@@ -211,6 +232,7 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
           const uint32_t off = ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
           mma_ss_lh(tmem + buf * 128, q_lo + off, HI, ka + off, HI, IDESC_QK, ks > 0);
         }
+        BW_TRACE_AT(true, 24, g);
         tc_commit(&bars.s_full[buf]);
         tc_commit(&bars.kv_empty[e % NS]);
         if (j == n - 1) tc_commit(&bars.q_empty);
@@ -239,21 +261,24 @@ __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
     for (int sg = 0; ok && sg < it.nseg; ++sg) {
       const int n = sg == 0 ? it.n[0] : it.n[1];
       for (int j = 0; j < n; ++j) {
-        const uint32_t g = tc + j, buf = g & 1;
+        constexpr uint32_t NB = Split<D>::NB;
+        const uint32_t g = tc + j, buf = g % NB;
         const uint32_t e = e0 + pos_v(j, n);
         if (!wc.wait(&bars.kv_full[e % NS], (e / NS) & 1)) { ok = false; break; }
         // the previous tile's epilogue must have read O before PV(0) overwrites it
         if (j == 0 && itn > 0 && !wc.wait(&bars.o_empty, (itn - 1) & 1)) { ok = false; break; }
-        if (!issuer_wait(wc, &bars.p_full[buf], (g >> 1) & 1)) { ok = false; break; }
+        if (!issuer_wait(wc, &bars.p_full[buf], (g / NB) & 1)) { ok = false; break; }
         BW_TRACE_AT(true, 6, g);
         tc_fence_after();
         const uint32_t va = v_lo0 + (e % NS) * (uint32_t)(L::kTile / 16);
-        // half h: O_h += P_h (TMEM columns 64 h .. 64 h + 31 of the buffer) * V rows 64 h .. 64 h + 63
+        // part q: O_q += P_q (TMEM columns q K .. q K + K/2 - 1 of the buffer, K = keys
+        // per part) * V rows q K .. q K + K - 1; k-step ks covers V rows 16 ks .. 16 ks + 15
+        constexpr int KSP = Split<D>::kKeys / 16;   // k-steps per part
 #pragma unroll
         for (int ks = 0; ks < kRows / 16; ++ks) {
-          const int h = ks >> 2;
-          mma_ts_lh(tmem + 256 + h * D, tmem + buf * 128 + h * 64 + (ks & 3) * 8, va + (ks * 16 * 128) / 16, HI,
-                    IDESC_PV, ((ks & 3) > 0 || j > 0) ? 1u : 0u);
+          const int q = ks / KSP, kin = ks % KSP;
+          mma_ts_lh(tmem + Split<D>::kOCol + q * D, tmem + buf * 128 + q * Split<D>::kKeys + kin * 8, va + (ks * 16 * 128) / 16,
+                    HI, IDESC_PV, (kin > 0 || j > 0) ? 1u : 0u);
         }
         BW_TRACE_AT(true, 8, g);
         tc_commit(&bars.pv_done[buf]);
@@ -276,13 +301,18 @@ __device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
 }
 
 // ----------------------------------------------------------- softmax warps
-// Thread t (0..255): row t % 128 of the item's tile (TMEM lane), half t / 128.
+// Thread t (0 .. 128 N - 1): row t % 128 of the item's tile (TMEM lane), part
+// t / 128, i.e. keys part K .. part K + K - 1 of every key tile (K = 128 / N).
 template <int D, int POLY>
 __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
   using L = L3<D>;
-  const int rl = t & 127, half = t >> 7;
+  constexpr int N = Split<D>::N;
+  constexpr int K = Split<D>::kKeys;
+  constexpr int DC = D / N;                 // output columns this thread writes
+  const int rl = t & 127, part = t >> 7;
   const uint32_t lane_off = (uint32_t)((rl >> 5) * 32) << 16;
-  const uint32_t o_own = tmem + lane_off + 256 + half * D;
+  constexpr uint32_t NB = Split<D>::NB;
+  const uint32_t o_own = tmem + lane_off + Split<D>::kOCol + part * D;
   const float c = p.scale_log2;
   float2* xch = reinterpret_cast<float2*>(smem + L::kX);
   uint32_t tc = 0, itn = 0;
@@ -295,22 +325,23 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
     const int row = qt * kRows + rl;
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; j < n; ++j) {
-      const uint32_t g = tc + j, buf = g & 1;
-      const uint32_t s_tmem = tmem + lane_off + buf * 128 + half * 64;
-      if (!wc.wait(&bars.s_full[buf], (g >> 1) & 1)) return;
+      const uint32_t g = tc + j, buf = g % NB;
+      const uint32_t s_tmem = tmem + lane_off + buf * 128 + part * K;
+      if (!wc.wait(&bars.s_full[buf], (g / NB) & 1)) return;
       BW_TRACE_AT(t == 0, 0, g);
       BW_TRACE_AT(t == 128, 4, g);
       tc_fence_after();
-      uint32_t r[64];
-      tmem_ld64(s_tmem, r);
+      uint32_t r[K];
+      if constexpr (K == 64) tmem_ld64(s_tmem, r);
+      else tmem_ld32(s_tmem, r);
       BW_TRACE_AT(t == 0, 1, g);
       float* s = reinterpret_cast<float*>(r);
-      const int kv0 = j * kRows + half * 64;
-      if ((p.causal && kv0 + 63 > qt * kRows) || kv0 + 64 > p.Skv) {
+      const int kv0 = j * kRows + part * K;
+      if ((p.causal && kv0 + K - 1 > qt * kRows) || kv0 + K > p.Skv) {
         int lim = p.Skv - kv0;
         if (p.causal) lim = min(lim, row + 1 - kv0);
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < K; ++i)
           if (i >= lim) s[i] = -INFINITY;
       }
       float mx;
@@ -319,7 +350,7 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
 #pragma unroll
         for (int u = 0; u < 8; ++u) a[u] = fmaxf(s[u], s[8 + u]);
 #pragma unroll
-        for (int i = 16; i < 64; i += 16)
+        for (int i = 16; i < K; i += 16)
 #pragma unroll
           for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
         mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
@@ -335,7 +366,7 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
       const f2 cc2{c, c}, nm2{-msub, -msub};
       f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
+      for (int k = 0; k < K / 2; ++k) {
         const f2 x = ffma2(f2{s[2 * k], s[2 * k + 1]}, cc2, nm2);
         f2 e;
         if ((k & 7) < POLY) {
@@ -355,14 +386,15 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
       l_run = l_run * corr + (acc0.x + acc0.y);
       BW_TRACE_AT(t == 0, 2, g);
       {
-        uint32_t pk[32];
+        uint32_t pk[K / 2];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) pk[k] = pack_bf16_3(s[2 * k], s[2 * k + 1]);
-        tmem_st32(s_tmem, pk);
+        for (int k = 0; k < K / 2; ++k) pk[k] = pack_bf16_3(s[2 * k], s[2 * k + 1]);
+        if constexpr (K == 64) tmem_st32(s_tmem, pk);
+        else tmem_st16(s_tmem, pk);
       }
       if (j > 0 && __any_sync(0xffffffffu, upd)) {
-        // O_h must hold PV(j - 1) before it is rescaled
-        if (!wc.wait(&bars.pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1)) return;
+        // O_part must hold PV(j - 1) before it is rescaled
+        if (!wc.wait(&bars.pv_done[(g - 1) % NB], ((g - 1) / NB) & 1)) return;
         tc_fence_after();
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
@@ -378,46 +410,66 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
       mbar_arrive(&bars.p_full[buf]);
       BW_TRACE_AT(t == 0, 3, g);
       BW_TRACE_AT(t == 128, 5, g);
-      BW_TRACE_AT((t & 31) == 0 && t < 128, 10 + (t >> 5), g);
-      BW_TRACE_AT((t & 31) == 0 && t >= 128, 14 + ((t - 128) >> 5), g);
+      BW_TRACE_AT((t & 31) == 0 && t < 256, 10 + (t >> 5), g);
     }
-    // merge the two halves of the row: exchange (m, l) through shared memory
-    xch[half * kRows + rl] = make_float2(m_run, l_run);
+    // merge the parts of the row: exchange (m, l) through shared memory
+    xch[part * kRows + rl] = make_float2(m_run, l_run);
     mbar_arrive(&bars.xch);
     if (!wc.wait(&bars.xch, itn & 1)) return;
-    const float2 other = xch[(half ^ 1) * kRows + rl];
-    const float m0 = half == 0 ? m_run : other.x, l0 = half == 0 ? l_run : other.y;
-    const float m1 = half == 0 ? other.x : m_run, l1 = half == 0 ? other.y : l_run;
-    const float m = fmaxf(m0, m1);
-    const float w0 = m0 == -INFINITY ? 0.f : ex2_mufu(m0 - m);
-    const float w1 = m1 == -INFINITY ? 0.f : ex2_mufu(m1 - m);
-    const float lsum = l0 * w0 + l1 * w1;
+    float mp[N], lp[N];
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+      const float2 v = xch[q * kRows + rl];
+      mp[q] = v.x;
+      lp[q] = v.y;
+    }
+    float m = mp[0];
+#pragma unroll
+    for (int q = 1; q < N; ++q) m = fmaxf(m, mp[q]);
+    float wq[N], lsum = 0.f;
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+      wq[q] = mp[q] == -INFINITY ? 0.f : ex2_mufu(mp[q] - m);
+      lsum = fmaf(lp[q], wq[q], lsum);
+    }
     const float inv_l = 1.f / lsum;
-    const float a0 = w0 * inv_l, a1 = w1 * inv_l;
+#pragma unroll
+    for (int q = 0; q < N; ++q) wq[q] *= inv_l;
     if (!wc.wait(&bars.o_full, itn & 1)) return;
     tc_fence_after();
-    // this thread writes output columns [half * D/2, half * D/2 + D/2)
-    const uint32_t o0 = tmem + lane_off + 256 + half * (D / 2);
-    uint32_t q[D / 4];
+    // this thread writes output columns [part DC, part DC + DC) = sum over q of O_q * w_q
+    const uint32_t o0 = tmem + lane_off + Split<D>::kOCol + part * DC;
+    float acc[DC];
 #pragma unroll
-    for (int c0 = 0; c0 < D / 2; c0 += 32) {
-      uint32_t x0[32], x1[32];
-      tmem_ld32(o0 + c0, x0);
-      tmem_ld32(o0 + D + c0, x1);
+    for (int i = 0; i < DC; ++i) acc[i] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        q[c0 / 2 + i] = pack_bf16_3(__uint_as_float(x0[2 * i]) * a0 + __uint_as_float(x1[2 * i]) * a1,
-                                    __uint_as_float(x0[2 * i + 1]) * a0 + __uint_as_float(x1[2 * i + 1]) * a1);
+    for (int q = 0; q < N; ++q) {
+#pragma unroll
+      for (int c0 = 0; c0 < DC; c0 += (DC < 32 ? DC : 32)) {
+        if constexpr (DC >= 32) {
+          uint32_t x[32];
+          tmem_ld32(o0 + q * D + c0, x);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
+        } else {
+          uint32_t x[16];
+          tmem_ld16(o0 + q * D + c0, x);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
+        }
+      }
     }
     // O has been read: the next item's first PV may overwrite it
     tc_fence_before();
     mbar_arrive(&bars.o_empty);
     if (row < p.Sq) {
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.O) + it.b * p.o_sb + it.h * p.o_sh +
-                                            (int64_t)row * p.o_ss + half * (D / 2));
+                                            (int64_t)row * p.o_ss + part * DC);
 #pragma unroll
-      for (int i = 0; i < D / 16; ++i) dst[i] = make_uint4(q[4 * i], q[4 * i + 1], q[4 * i + 2], q[4 * i + 3]);
-      if (p.LSE != nullptr && half == 0)
+      for (int i = 0; i < DC / 8; ++i)
+        dst[i] = make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
+                            pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
+      if (p.LSE != nullptr && part == 0)
         p.LSE[((int64_t)it.b * p.Hq + it.h) * p.Sq + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
     }
     tc += n;
@@ -426,10 +478,8 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
   }
 }
 
-constexpr int kThreads3 = 352;
-
 template <int D, int POLY>
-__global__ void __launch_bounds__(kThreads3, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
+__global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
   using L = L3<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -437,20 +487,21 @@ __global__ void __launch_bounds__(kThreads3, 1) fmha_fwd3_kernel(const FmhaParam
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  constexpr int kSoftWarps = 4 * Split<D>::N;
+  constexpr int kProducer = kSoftWarps, kPvIssuer = kSoftWarps + 1;
 
   if (tid == 0) {
     mbar_init(&bars.q_full, 1);
     mbar_init(&bars.q_empty, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Split<D>::NB; ++b) {
       mbar_init(&bars.s_full[b], 1);
-      mbar_init(&bars.p_full[b], 256);
+      mbar_init(&bars.p_full[b], 128 * Split<D>::N);
     }
-    mbar_init(&bars.pv_done[0], 1);
-    mbar_init(&bars.pv_done[1], 1);
+    for (int b = 0; b < Split<D>::NB; ++b) mbar_init(&bars.pv_done[b], 1);
     mbar_init(&bars.qk_done, 1);
     mbar_init(&bars.o_full, 1);
-    mbar_init(&bars.o_empty, 256);
-    mbar_init(&bars.xch, 256);
+    mbar_init(&bars.o_empty, 128 * Split<D>::N);
+    mbar_init(&bars.xch, 128 * Split<D>::N);
     mbar_init(&bars.mma_done, 1);
     for (int s = 0; s < L::NS; ++s) {
       mbar_init(&bars.kv_full[s], 1);
@@ -459,31 +510,31 @@ __global__ void __launch_bounds__(kThreads3, 1) fmha_fwd3_kernel(const FmhaParam
     bars.abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == kProducer && lane == 0) {
     prefetch_tmap(&maps.q);
     prefetch_tmap(&maps.k);
     prefetch_tmap(&maps.v);
   }
-  if (warp == 9) tmem_alloc(&bars.tmem_base, 512);
+  if (warp == kPvIssuer) tmem_alloc(&bars.tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars.tmem_base;
   WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, warp};
 
-  if (warp < 8) {
+  if (warp < kSoftWarps) {
     softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
-  } else if (warp == 8) {
+  } else if (warp == kProducer) {
     if (lane == 0) producer3<D>(p, maps, smem, bars, wc);
   } else {
     if (lane == 0) {
-      if (warp == 9) pv_issuer3<D>(p, smem, bars, wc, tmem);
+      if (warp == kPvIssuer) pv_issuer3<D>(p, smem, bars, wc, tmem);
       else qk_issuer3<D>(p, smem, bars, wc, tmem);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kPvIssuer) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -496,7 +547,7 @@ cudaError_t launch3(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cuda
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
   const int grid = p.num_items < num_sms ? p.num_items : num_sms;
-  kern<<<grid, kThreads3, bytes, stream>>>(p, maps);
+  kern<<<grid, Split<D>::kThreads, bytes, stream>>>(p, maps);
   return cudaGetLastError();
 }
 
