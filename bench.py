@@ -409,14 +409,13 @@ def run_ours(args, world, rank, local):
     hq_, hk_, hv_ = (x.cpu().pin_memory() for x in (q, k, v))
     ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
     hl = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    bufs = (dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2), o.transpose(1, 2), lse)
+    ws = torch.empty(bw.host_workspace_size(B, Hq, Hkv, S, D), dtype=torch.uint8, device=dev)
 
     def e2e_step():
-        # public host-buffer API: batch chunks pipelined over copy-in, compute and
-        # copy-out streams (PCIe in / out and the kernel overlap)
+        # public host-buffer C-ABI call (bw_attn_fwd_host): copy-in, kernel and
+        # copy-out pipelined in sequence chunks (PCIe in / out and the kernel overlap)
         bw.attention_from_host(hq_.transpose(1, 2), hk_.transpose(1, 2), hv_.transpose(1, 2), ho.transpose(1, 2),
-                               hl, scale=scale, causal=True, chunks=4, buffers=bufs)
+                               hl, scale=scale, causal=True, chunks=args.e2e_chunks, workspace=ws)
 
     ms_e2e = time_steps(e2e_step, e2e_steps, 2, lambda: None, world)
     e2e_ms_max = max_over_ranks(sum(ms_e2e), world)
@@ -426,7 +425,7 @@ def run_ours(args, world, rank, local):
 
     secondary = {}
     if rank == 0 and world == 1 and not (args.no_secondary or args.profile):
-        del hq_, hk_, hv_, dq, dk, dv
+        del hq_, hk_, hv_, ws
         torch.cuda.empty_cache()
         sec_steps = max(5, min(args.steps // 10, 50))
         secondary["C3_mha_D64"] = bench_prefill((8, 16, 16, 2048, 64), False, "bhsd", flush, sec_steps, 3)
@@ -499,6 +498,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="pieces the host-buffer e2e call pipelines (sequence chunks for causal C2)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")

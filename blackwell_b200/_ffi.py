@@ -12,6 +12,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libbw_attn.so"
 
 BW_OK, BW_ERR_SHAPE, BW_ERR_ALIGN, BW_ERR_CUDA, BW_ERR_TIMEOUT, BW_ERR_NCCL, BW_ERR_NULL, BW_ERR_WORKSPACE = range(8)
+BW_LAYOUT_BHSD, BW_LAYOUT_BSHD = 0, 1
 BW_OPT_TIMEOUT_NS, BW_OPT_P_IN_TMEM, BW_OPT_DEBUG_FLAGS, BW_OPT_MAX_CTAS, BW_OPT_EXP_POLY, BW_OPT_PREFILL_KERNEL = 1, 2, 3, 4, 5, 6
 
 # Every symbol the header declares, with (restype, argtypes).
@@ -41,6 +42,8 @@ SIGNATURES = {
     "bw_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     "bw_qk_norm_rope": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _f, _i, _vp, _vp]),
     "bw_gqa_fused_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "bw_attn_fwd_host_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "bw_attn_fwd_host": (_i, [_vp] * 5 + [_i] * 5 + [_f, _i, _i, _i, _vp, _sz, _vp]),
     "bw_gqa_fused_fwd": (_i, [_vp] * 10 + [_i] * 8 + [_f, _i, _f, _i, _vp, _sz, _vp]),
     "bw_stream_status": (_i, [_vp]),
     "bw_set_option": (_i, [_i, _i64]),

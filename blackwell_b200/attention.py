@@ -278,64 +278,54 @@ def gqa_fused_fwd(q, k, v, cos_sin_cache, q_gamma=None, k_gamma=None, eps=1e-6, 
     return o, lse, qr, kr
 
 
-_PIPE = {}
+def _host_layout(t):
+    """BW_LAYOUT_BHSD / BW_LAYOUT_BSHD for a contiguous host tensor seen as [B, H, S, D]."""
+    B, H, S, D = t.shape
+    st = t.stride()
+    if st == (H * S * D, S * D, D, 1):
+        return _ffi.BW_LAYOUT_BHSD
+    if st == (S * H * D, D, H * D, 1):
+        return _ffi.BW_LAYOUT_BSHD
+    return None
 
 
-def _pipe_streams(device):
-    """Per-device copy-in / compute / copy-out streams for the host-buffer path."""
-    key = device.index if device.index is not None else torch.cuda.current_device()
-    if key not in _PIPE:
-        with torch.cuda.device(key):
-            _PIPE[key] = (torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream())
-    return _PIPE[key]
+def host_workspace_size(B, Hq, Hkv, S, D):
+    """Device bytes `attention_from_host` needs for its copies of Q, K, V, O, LSE."""
+    return int(_ffi.lib().bw_attn_fwd_host_workspace_size(B, Hq, Hkv, S, D))
 
 
 def attention_from_host(q_host, k_host, v_host, o_host, lse_host=None, scale=None, causal=False, chunks=4,
-                        device=None, buffers=None):
-    """Attention forward on HOST tensors (pinned for overlap) through the device.
+                        workspace=None):
+    """Attention forward on HOST tensors through `bw_attn_fwd_host`.
 
-    q/k/v/o_host: [B, H, S, D] views (BHSD or BSHD via strides) on the host, bf16;
-    lse_host: fp32 [B, Hq, S] or None.  The batch is cut into `chunks` pieces:
-    copy-in of piece i+1, the kernel on piece i and copy-out of piece i-1 run on
-    three streams at once, so PCIe in, PCIe out and the tensor cores overlap.
-    `buffers` (device tensors shaped like the inputs) may be passed to reuse
-    device memory across calls.  Returns when the caller's current stream has
-    the whole result ordered after it (same as the other calls: asynchronous)."""
-    device = device or torch.device("cuda", torch.cuda.current_device())
-    B = q_host.shape[0]
-    chunks = max(1, min(chunks, B))
-    if buffers is None:
-        buffers = tuple(torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=device)
-                        for t in (q_host, k_host, v_host, o_host))
-        lse_d = torch.empty(lse_host.shape, dtype=torch.float32, device=device) if lse_host is not None else None
-        buffers = buffers + (lse_d,)
-    dq, dk, dv, do, dl = buffers
-    s_in, s_cmp, s_out = _pipe_streams(device)
-    cur = torch.cuda.current_stream(device)
-    s_in.wait_stream(cur)
-    bounds = [round(i * B / chunks) for i in range(chunks + 1)]
-    for i in range(chunks):
-        b0, b1 = bounds[i], bounds[i + 1]
-        if b0 == b1:
-            continue
-        with torch.cuda.stream(s_in):
-            for d, h in ((dq, q_host), (dk, k_host), (dv, v_host)):
-                d[b0:b1].copy_(h[b0:b1], non_blocking=True)
-            ev_in = torch.cuda.Event()
-            ev_in.record(s_in)
-        s_cmp.wait_event(ev_in)
-        with torch.cuda.stream(s_cmp):
-            _attn(dq[b0:b1], dk[b0:b1], dv[b0:b1], scale, causal, out=do[b0:b1],
-                  lse=dl[b0:b1] if dl is not None else None, return_lse=dl is not None)
-            ev_c = torch.cuda.Event()
-            ev_c.record(s_cmp)
-        s_out.wait_event(ev_c)
-        with torch.cuda.stream(s_out):
-            o_host[b0:b1].copy_(do[b0:b1], non_blocking=True)
-            if lse_host is not None:
-                lse_host[b0:b1].copy_(dl[b0:b1], non_blocking=True)
-    cur.wait_stream(s_out)
-    cur.wait_stream(s_cmp)
+    q/k/v/o_host: [B, H, S, D] views of contiguous BHSD or BSHD host tensors
+    (bf16; page-locked for the copies to overlap); lse_host: fp32 [B, Hq, S]
+    or None.  The library cuts the work into `chunks` pieces and overlaps
+    copy-in, the kernel and copy-out (causal: along the sequence, otherwise
+    along the batch).  `workspace`: a uint8 CUDA tensor of at least
+    `host_workspace_size(...)` bytes, reused across calls; allocated when None.
+    Asynchronous like the other calls: synchronise the current stream before
+    reading o_host / lse_host."""
+    B, Hq, S, D = q_host.shape
+    Hkv = k_host.shape[1]
+    layout = _host_layout(q_host)
+    if layout is None or any(_host_layout(t) != layout for t in (k_host, v_host, o_host)):
+        raise ValueError("host tensors must be contiguous BHSD or BSHD, all in the same layout")
+    for t in (q_host, k_host, v_host, o_host):
+        if t.is_cuda or t.dtype != torch.bfloat16:
+            raise ValueError("q/k/v/o_host must be bf16 host tensors")
+    if lse_host is not None and (lse_host.is_cuda or lse_host.dtype != torch.float32 or not lse_host.is_contiguous()
+                                 or tuple(lse_host.shape) != (B, Hq, S)):
+        raise ValueError("lse_host must be a contiguous fp32 host tensor [B, Hq, S]")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    need = host_workspace_size(B, Hq, Hkv, S, D)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=torch.device("cuda", torch.cuda.current_device()))
+    rc = _ffi.lib().bw_attn_fwd_host(_ptr(q_host), _ptr(k_host), _ptr(v_host), _ptr(o_host), _ptr(lse_host),
+                                     B, Hq, Hkv, S, D, float(scale), int(bool(causal)), layout, int(chunks),
+                                     _ptr(workspace), workspace.numel(), _stream())
+    _ffi.check(rc, "bw_attn_fwd_host")
     return o_host, lse_host
 
 

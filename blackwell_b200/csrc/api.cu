@@ -102,8 +102,11 @@ void contiguous(int H, int S, int D, int64_t out[3]) {
   out[0] = (int64_t)H * S * D;
 }
 
+// q_offset: causal query row i is sequence row q_offset + i (multiple of 128);
+// lse_sh: LSE stride between heads (0 = Sq).
 int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int Sq,
-             int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream) {
+             int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream,
+             int q_offset = 0, int lse_sh = 0) {
   if (!Q || !K || !V || !O) return BW_ERR_NULL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0 || G <= 0) return BW_ERR_SHAPE;
   if (Hq % Hkv != 0 || Hq / Hkv != G) return BW_ERR_SHAPE;
@@ -126,8 +129,10 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   int rc = get_device_state(&dev);
   if (rc != BW_OK) return rc;
 
+  if (q_offset < 0 || (q_offset & 127) || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
   int kern = (int)g_prefill_kernel.load();
   if (kern == 0) kern = D == 128 ? 3 : 1;
+  if (kern == 2 && q_offset != 0) kern = 1;   // kernel 2 has no query offset
   const bool v2 = kern == 2;
   const uint32_t kv_rows = v2 ? 64u : 128u;
   bw::FmhaMaps maps;
@@ -158,6 +163,8 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   p.err = dev->err;
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.debug_flags = (int)g_debug_flags.load();
+  p.q_offset = q_offset;
+  p.lse_sh = lse_sh > 0 ? lse_sh : Sq;
   int ctas = dev->num_sms;
   const int64_t cap = g_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = (int)cap;
@@ -179,6 +186,12 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace
 
 namespace bw {
+
+int attn_forward(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int Sq,
+                 int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream,
+                 int q_offset, int lse_sh) {
+  return attn_fwd(Q, K, V, O, LSE, B, Hq, Hkv, Sq, Skv, G, D, scale, causal, strides, stream, q_offset, lse_sh);
+}
 int device_context(int** err, int* num_sms, void** encode_fn) {
   DeviceState* dev = nullptr;
   const int rc = get_device_state(&dev);
@@ -274,6 +287,8 @@ int bw_mha_fwd_f32(const float* Q, const float* K, const float* V, float* O, flo
   p.err = dev->err;
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.debug_flags = 0;
+  p.q_offset = 0;
+  p.lse_sh = S;
   cudaError_t e = bw::launch_fmha_fwd_f32(p, maps, dev->num_sms, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }

@@ -115,7 +115,7 @@ __device__ __forceinline__ Item decode_item(const FmhaParams& p, int idx) {
   for (int w = 0; w < 2; ++w) {
     const int t = it.qt[w];
     int n = 0;
-    if (t < p.n_qtiles) n = p.causal ? min(t + 1, p.n_kvtiles) : p.n_kvtiles;
+    if (t < p.n_qtiles) n = p.causal ? min(t + 1 + (p.q_offset >> 7), p.n_kvtiles) : p.n_kvtiles;
     it.nkv[w] = n;
   }
   it.nmax = max(it.nkv[0], it.nkv[1]);
@@ -335,10 +335,10 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
       tmem_ld128(s_tmem, r);
       float* s = reinterpret_cast<float*>(r);
       const int kv0 = j * kRows;
-      const bool diag = p.causal && (kv0 + kRows - 1 > it.qt[w] * kRows);
+      const bool diag = p.causal && (kv0 + kRows - 1 > p.q_offset + it.qt[w] * kRows);
       if (diag || kv0 + kRows > p.Skv) {
         int lim = p.Skv - kv0;
-        if (p.causal) lim = min(lim, row + 1 - kv0);
+        if (p.causal) lim = min(lim, p.q_offset + row + 1 - kv0);
 #pragma unroll
         for (int i = 0; i < 128; ++i)
           if (i >= lim) s[i] = -INFINITY;
@@ -467,7 +467,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
       }
     }
     if (p.LSE != nullptr && row < p.Sq)
-      p.LSE[((int64_t)it.b * p.Hq + h) * p.Sq + row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
+      p.LSE[((int64_t)it.b * p.Hq + h) * p.lse_sh + row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
     tc_fence_before();
   }
 }

@@ -378,7 +378,7 @@ __device__ void softmax2(const FmhaParams& p, Bars2& bars, const WaitCtl& wc, ui
       }
     }
     if (p.LSE != nullptr && row < p.Sq)
-      p.LSE[((int64_t)it.b * p.Hq + h) * p.Sq + row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
+      p.LSE[((int64_t)it.b * p.Hq + h) * p.lse_sh + row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
     tc_fence_before();
   }
 }

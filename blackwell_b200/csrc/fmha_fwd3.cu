@@ -110,8 +110,8 @@ __device__ __forceinline__ Item3 decode_item3(const FmhaParams& p, int idx) {
     it.qt[0] = p.n_qtiles - 1 - u;
     it.qt[1] = u;
     it.nseg = it.qt[1] == it.qt[0] ? 1 : 2;
-    it.n[0] = min(it.qt[0] + 1, p.n_kvtiles);
-    it.n[1] = min(it.qt[1] + 1, p.n_kvtiles);
+    it.n[0] = min(it.qt[0] + 1 + (p.q_offset >> 7), p.n_kvtiles);
+    it.n[1] = min(it.qt[1] + 1 + (p.q_offset >> 7), p.n_kvtiles);
   } else {
     it.qt[0] = it.qt[1] = u;
     it.nseg = 1;
@@ -337,9 +337,9 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
       BW_TRACE_AT(t == 0, 1, g);
       float* s = reinterpret_cast<float*>(r);
       const int kv0 = j * kRows + part * K;
-      if ((p.causal && kv0 + K - 1 > qt * kRows) || kv0 + K > p.Skv) {
+      if ((p.causal && kv0 + K - 1 > p.q_offset + qt * kRows) || kv0 + K > p.Skv) {
         int lim = p.Skv - kv0;
-        if (p.causal) lim = min(lim, row + 1 - kv0);
+        if (p.causal) lim = min(lim, p.q_offset + row + 1 - kv0);
 #pragma unroll
         for (int i = 0; i < K; ++i)
           if (i >= lim) s[i] = -INFINITY;
@@ -470,7 +470,7 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
         dst[i] = make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
                             pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
       if (p.LSE != nullptr && part == 0)
-        p.LSE[((int64_t)it.b * p.Hq + it.h) * p.Sq + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
+        p.LSE[((int64_t)it.b * p.Hq + it.h) * p.lse_sh + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
     }
     tc += n;
     ++itn;

@@ -4,6 +4,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "../../include/bw_attn.h"
+
 namespace bw {
 
 // Prefill / full-sequence attention forward (GQA, MHA = GQA with G = 1).
@@ -21,6 +23,10 @@ struct FmhaParams {
   int* err;                      // device error word
   uint64_t timeout_ns;           // bound for every device-side wait
   int debug_flags;               // bit 0: producer withholds its first K load (timeout test)
+  int q_offset;                  // causal: query row i is sequence row q_offset + i (multiple of 128;
+                                 // key j visible iff j <= q_offset + i); 0 = top-left alignment
+  int lse_sh;                    // LSE element stride between heads (>= Sq); LSE[b][h][i] at
+                                 // (b * Hq + h) * lse_sh + i
 };
 
 struct FmhaMaps {
@@ -107,6 +113,12 @@ struct NormRopeParams {
 };
 
 cudaError_t launch_norm_rope(const NormRopeParams& p, int num_sms, cudaStream_t stream);
+
+// The attention forward of the C ABI with the internal extras: causal query
+// offset (multiple of 128) and LSE head stride (0 = Sq).  Returns a status code.
+int attn_forward(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int Sq,
+                 int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream,
+                 int q_offset, int lse_sh);
 
 // Per-device state owned by api.cu: the device error word, the SM count and the
 // driver's cuTensorMapEncodeTiled.  Returns a bw_attn status code.

@@ -187,6 +187,26 @@ BW_API int bw_gqa_fused_fwd(const void* Q, const void* K, const void* V, void* O
                             int pos_offset, float eps, int interleaved, float scale, int causal, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* Host tensor layouts for bw_attn_fwd_host. */
+enum { BW_LAYOUT_BHSD = 0, BW_LAYOUT_BSHD = 1 };
+
+/* Attention forward on HOST buffers: the reference harness's copy-in /
+ * launch / copy-out sequence (kernelBench.cuh:34-98 around launch_gqa_vN,
+ * GQA_sm103_causal_v3.cu:2156-2180) as one call, with the PCIe copies
+ * pipelined against the kernels in `chunks` pieces (<= 32; 0 = 4): causal
+ * calls are cut along the sequence (query rows [s0, s1) need keys [0, s1)
+ * only), non-causal calls along the batch.  Q, K, V, O are contiguous host
+ * tensors in `layout` (BHSD or BSHD), LSE host [B, Hq, S] fp32 or NULL.
+ * `workspace` (device, 256-byte aligned, bw_attn_fwd_host_workspace_size
+ * bytes) holds the device copies.  Asynchronous: O and LSE are complete when
+ * `stream` reaches this point (synchronise it before reading them).  The
+ * copies overlap only if the host buffers are page-locked.  Calls on one
+ * device are serialised inside the library while they enqueue. */
+BW_API size_t bw_attn_fwd_host_workspace_size(int B, int Hq, int Hkv, int S, int D);
+BW_API int bw_attn_fwd_host(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv,
+                            int S, int D, float scale, int causal, int layout, int chunks, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Synchronise `stream`, then read and clear this device's error word.
  * Returns BW_OK, BW_ERR_TIMEOUT, BW_ERR_WORKSPACE or BW_ERR_CUDA. */
 BW_API int bw_stream_status(void* stream);

@@ -189,23 +189,30 @@ def test_long_context_rows():
     assert np.abs(np.array([lc[b, h, i] for b, h, i in rows]) - rl).max() <= LSE_TOL
 
 
-@pytest.mark.parametrize("chunks", [1, 3])
-def test_attention_from_host_pipelined(chunks):
-    """Host-buffer path (chunked copy-in / compute / copy-out on three streams)
-    gives the same bits as the device path."""
+@pytest.mark.parametrize("layout,causal,S,chunks,D", [
+    ("bshd", True, 320, 1, 128), ("bshd", True, 320, 3, 128), ("bshd", True, 1000, 8, 128),
+    ("bhsd", True, 777, 4, 128), ("bshd", False, 320, 3, 128), ("bhsd", False, 200, 2, 128),
+    ("bhsd", True, 64, 4, 128), ("bshd", True, 1000, 5, 64), ("bhsd", True, 513, 3, 64),
+])
+def test_attention_from_host_pipelined(layout, causal, S, chunks, D):
+    """bw_attn_fwd_host (copy-in / kernel / copy-out pipelined in sequence or
+    batch chunks; causal chunks run with a query offset) gives the same bits as
+    the device path."""
     import blackwell_b200 as bw
-    B, S, Hq, Hkv, D = 3, 320, 8, 2, 128
-    q = seeded_bf16((B, S, Hq, D), 61).pin_memory()
-    k = seeded_bf16((B, S, Hkv, D), 62).pin_memory()
-    v = seeded_bf16((B, S, Hkv, D), 63).pin_memory()
-    o = torch.empty(B, S, Hq, D, dtype=torch.bfloat16).pin_memory()
+    B, Hq, Hkv = 3, 8, 2
+    shp = (lambda h: (B, S, h, D)) if layout == "bshd" else (lambda h: (B, h, S, D))
+    view = (lambda t: t.transpose(1, 2)) if layout == "bshd" else (lambda t: t)
+    q = seeded_bf16(shp(Hq), 61).pin_memory()
+    k = seeded_bf16(shp(Hkv), 62).pin_memory()
+    v = seeded_bf16(shp(Hkv), 63).pin_memory()
+    o = torch.empty(shp(Hq), dtype=torch.bfloat16).pin_memory()
     lse = torch.empty(B, Hq, S, dtype=torch.float32).pin_memory()
-    bw.attention_from_host(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), o.transpose(1, 2), lse,
-                           causal=True, chunks=chunks)
+    bw.attention_from_host(view(q), view(k), view(v), view(o), lse, causal=causal, chunks=chunks)
     torch.cuda.synchronize()
     assert bw.stream_status() == 0
-    ro, rl = bw.gqa_causal_fwd(q.cuda().transpose(1, 2), k.cuda().transpose(1, 2), v.cuda().transpose(1, 2))
-    assert torch.equal(o.transpose(1, 2), ro.cpu()) and torch.equal(lse, rl.cpu())
+    fn = bw.gqa_causal_fwd if causal else bw.gqa_fwd
+    ro, rl = fn(view(q.cuda()), view(k.cuda()), view(v.cuda()))
+    assert torch.equal(view(o), ro.cpu()) and torch.equal(lse, rl.cpu())
 
 
 def test_mha_fp32_golden(golden):
