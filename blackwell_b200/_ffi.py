@@ -42,6 +42,7 @@ SIGNATURES = {
     "bw_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     "bw_qk_norm_rope": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _f, _i, _vp, _vp]),
     "bw_gqa_fused_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "bw_gqa_causal_offset_fwd": (_i, [_vp] * 5 + [_i] * 7 + [_f, _i, _vp, _vp]),
     "bw_attn_fwd_host_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "bw_attn_fwd_host": (_i, [_vp] * 5 + [_i] * 5 + [_f, _i, _i, _i, _vp, _sz, _vp]),
     "bw_gqa_fused_fwd": (_i, [_vp] * 10 + [_i] * 8 + [_f, _i, _f, _i, _vp, _sz, _vp]),

@@ -87,6 +87,23 @@ def gqa_split_fwd(q, k, v, scale=None, causal=False, out=None, lse=None):
     return _attn(q, k, v, scale, causal, out, lse)
 
 
+def gqa_causal_offset_fwd(q, k, v, q_offset, scale=None, out=None, lse=None):
+    """Causal GQA of a chunk of queries against a longer key prefix: query row i
+    is sequence position q_offset + i and sees keys j <= q_offset + i (chunked
+    prefill; with Skv = q_offset + Sq the bottom-right-aligned mask) -> (O, LSE)."""
+    B, Hq, Hkv, Sq, Skv, D = _check_inputs(q, k, v)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o = out if out is not None else torch.empty((B, Hq, Sq, D), dtype=torch.bfloat16, device=q.device)
+    if lse is None:
+        lse = torch.empty((B, Hq, Sq), dtype=torch.float32, device=q.device)
+    rc = _ffi.lib().bw_gqa_causal_offset_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, Hq, Hkv, Sq, Skv,
+                                             Hq // Hkv, D, float(scale), int(q_offset), _strides(q, k, v, o),
+                                             _stream())
+    _ffi.check(rc, "bw_gqa_causal_offset_fwd")
+    return o, lse
+
+
 def mha_fwd(q, k, v, scale=None, out=None, lse=None):
     """MHA forward (Hq == Hkv) -> (O, LSE)."""
     if q.shape[1] != k.shape[1]:

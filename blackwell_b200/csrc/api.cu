@@ -102,7 +102,7 @@ void contiguous(int H, int S, int D, int64_t out[3]) {
   out[0] = (int64_t)H * S * D;
 }
 
-// q_offset: causal query row i is sequence row q_offset + i (multiple of 128);
+// q_offset: causal query row i is sequence row q_offset + i;
 // lse_sh: LSE stride between heads (0 = Sq).
 int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq, int Hkv, int Sq,
              int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream,
@@ -129,7 +129,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   int rc = get_device_state(&dev);
   if (rc != BW_OK) return rc;
 
-  if (q_offset < 0 || (q_offset & 127) || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
+  if (q_offset < 0 || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
   int kern = (int)g_prefill_kernel.load();
   if (kern == 0) kern = D == 128 ? 3 : 1;
   if (kern == 2 && q_offset != 0) kern = 1;   // kernel 2 has no query offset
@@ -219,6 +219,13 @@ int bw_gqa_split_fwd(const void* Q, const void* K, const void* V, void* O, float
                      int Sq, int Skv, int G, int D, float scale, int causal, const bw_strides* strides,
                      void* stream) {
   return attn_fwd(Q, K, V, O, LSE, B, Hq, Hkv, Sq, Skv, G, D, scale, causal, strides, stream);
+}
+
+int bw_gqa_causal_offset_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int Hq,
+                             int Hkv, int Sq, int Skv, int G, int D, float scale, int q_offset,
+                             const bw_strides* strides, void* stream) {
+  if (q_offset < 0 || (int64_t)q_offset + Sq > (int64_t(1) << 30)) return BW_ERR_SHAPE;
+  return attn_fwd(Q, K, V, O, LSE, B, Hq, Hkv, Sq, Skv, G, D, scale, 1, strides, stream, q_offset, 0);
 }
 
 int bw_mha_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int H, int S, int D,

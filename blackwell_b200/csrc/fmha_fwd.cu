@@ -115,7 +115,7 @@ __device__ __forceinline__ Item decode_item(const FmhaParams& p, int idx) {
   for (int w = 0; w < 2; ++w) {
     const int t = it.qt[w];
     int n = 0;
-    if (t < p.n_qtiles) n = p.causal ? min(t + 1 + (p.q_offset >> 7), p.n_kvtiles) : p.n_kvtiles;
+    if (t < p.n_qtiles) n = p.causal ? min((p.q_offset + t * kRows + kRows - 1) / kRows + 1, p.n_kvtiles) : p.n_kvtiles;
     it.nkv[w] = n;
   }
   it.nmax = max(it.nkv[0], it.nkv[1]);

@@ -110,8 +110,8 @@ __device__ __forceinline__ Item3 decode_item3(const FmhaParams& p, int idx) {
     it.qt[0] = p.n_qtiles - 1 - u;
     it.qt[1] = u;
     it.nseg = it.qt[1] == it.qt[0] ? 1 : 2;
-    it.n[0] = min(it.qt[0] + 1 + (p.q_offset >> 7), p.n_kvtiles);
-    it.n[1] = min(it.qt[1] + 1 + (p.q_offset >> 7), p.n_kvtiles);
+    it.n[0] = min((p.q_offset + it.qt[0] * kRows + kRows - 1) / kRows + 1, p.n_kvtiles);
+    it.n[1] = min((p.q_offset + it.qt[1] * kRows + kRows - 1) / kRows + 1, p.n_kvtiles);
   } else {
     it.qt[0] = it.qt[1] = u;
     it.nseg = 1;

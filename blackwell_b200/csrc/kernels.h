@@ -23,8 +23,8 @@ struct FmhaParams {
   int* err;                      // device error word
   uint64_t timeout_ns;           // bound for every device-side wait
   int debug_flags;               // bit 0: producer withholds its first K load (timeout test)
-  int q_offset;                  // causal: query row i is sequence row q_offset + i (multiple of 128;
-                                 // key j visible iff j <= q_offset + i); 0 = top-left alignment
+  int q_offset;                  // causal: query row i is sequence row q_offset + i (key j visible
+                                 // iff j <= q_offset + i); 0 = top-left alignment
   int lse_sh;                    // LSE element stride between heads (>= Sq); LSE[b][h][i] at
                                  // (b * Hq + h) * lse_sh + i
 };

@@ -79,6 +79,16 @@ BW_API int bw_gqa_split_fwd(const void* Q, const void* K, const void* V, void* O
                      int Sq, int Skv, int G, int D, float scale, int causal, const bw_strides* strides,
                      void* stream);
 
+/* Causal attention of a chunk of queries against a longer key prefix
+ * (chunked prefill / prefix caching): query row i is sequence position
+ * q_offset + i and sees keys j <= q_offset + i; with Skv = q_offset + Sq this
+ * is the bottom-right-aligned causal mask.  q_offset = 0 is bw_gqa_split_fwd
+ * with causal = 1.  Extends the reference's split-length launcher
+ * (adhitya_GQA.cu:199-213), which has no offset. */
+BW_API int bw_gqa_causal_offset_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B,
+                                    int Hq, int Hkv, int Sq, int Skv, int G, int D, float scale, int q_offset,
+                                    const bw_strides* strides, void* stream);
+
 /* MHA forward (G = 1), bf16 in/out, optional LSE.
  * Replaces mha_v3_tc<Br,Bc,D><<<(S/Br,B*H),32,smem>>>(Q,K,V,O,scale,S)
  * (src/SM120/attention/MHA_sm120.cu:64-71, launch :333-345), which is fp32

@@ -84,13 +84,16 @@ def fp64_reference(q, k, v, scale, causal=False):
     return out, lse
 
 
-def fp64_rows(q, k, v, scale, causal, rows):
+def fp64_rows(q, k, v, scale, causal, rows, q_offset=0):
     """Exact float64 output for a subset of query rows.
 
     ``rows`` is an int array [R, 3] of (b, hq, i).  Every query row of attention
     is independent, so this is the same arithmetic as ``fp64_reference`` restricted
     to those rows (used at the full config sizes, where the all-rows oracle would
-    take hours).  Returns O [R, D] float64 and LSE [R] float64."""
+    take hours).  ``q_offset`` (causal only) places query row i at sequence
+    position q_offset + i, so it sees keys j <= q_offset + i (the chunked-prefill
+    extension; 0 is the reference's top-left alignment).  Returns O [R, D]
+    float64 and LSE [R] float64."""
     q, k, v = _as64(q), _as64(k), _as64(v)
     Hq, Hkv = q.shape[1], k.shape[1]
     G = Hq // Hkv
@@ -99,7 +102,7 @@ def fp64_rows(q, k, v, scale, causal, rows):
         hkv = hq // G
         kk, vv = k[b, hkv], v[b, hkv]
         if causal:
-            kk, vv = kk[: i + 1], vv[: i + 1]
+            kk, vv = kk[: q_offset + i + 1], vv[: q_offset + i + 1]
         o, l = _row_attention(q[b, hq, i : i + 1], kk, vv, scale)
         outs.append(o[0])
         lses.append(l[0])

@@ -104,5 +104,5 @@ def test_package_exports():
     for name in ["gqa_fwd", "gqa_causal_fwd", "gqa_split_fwd", "mha_fwd", "gqa_decode", "gqa_decode_paged",
                  "gqa_decode_partial", "lse_combine", "qk_norm_rope", "gqa_fused_fwd", "sdpa_gqa", "sdpa_gqa_causal",
                  "stream_status", "set_option", "get_option", "shard_plan", "decode_workspace_size",
-                 "attention_from_host"]:
+                 "attention_from_host", "gqa_causal_offset_fwd", "host_workspace_size"]:
         assert callable(getattr(bw, name)), name

@@ -93,3 +93,18 @@ def test_lse_combine_empty_split():
     out, lse = orc.lse_combine_reference(o, l)
     np.testing.assert_allclose(out, 1.0)
     np.testing.assert_allclose(lse, l[0], rtol=1e-6)
+
+
+def test_fp64_rows_query_offset_matches_full_causal():
+    """fp64_rows with q_offset (query i at sequence position q_offset + i) gives
+    the tail rows of the top-left-aligned causal reference on the full sequence."""
+    rng = np.random.default_rng(5)
+    B, Hq, Hkv, S, D, off = 1, 2, 1, 40, 16, 25
+    q = rng.standard_normal((B, Hq, S, D))
+    k = rng.standard_normal((B, Hkv, S, D))
+    v = rng.standard_normal((B, Hkv, S, D))
+    full_o, full_l = orc.fp64_reference(q, k, v, 0.25, causal=True)
+    rows = np.array([[0, h, i] for h in range(Hq) for i in range(S - off)])
+    o, l = orc.fp64_rows(q[:, :, off:], k, v, 0.25, True, rows, q_offset=off)
+    np.testing.assert_allclose(o, full_o[0, :, off:].reshape(-1, D), rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(l, full_l[0, :, off:].reshape(-1), rtol=1e-6, atol=1e-6)

@@ -215,6 +215,31 @@ def test_attention_from_host_pipelined(layout, causal, S, chunks, D):
     assert torch.equal(view(o), ro.cpu()) and torch.equal(lse, rl.cpu())
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("q_offset,Sq,Skv", [(0, 200, 200), (1, 130, 131), (77, 300, 377), (128, 256, 384),
+                                               (300, 129, 1000), (1000, 64, 1064)])
+def test_causal_offset(D, q_offset, Sq, Skv):
+    """Chunked-prefill causal mask (query i sees keys j <= q_offset + i) against
+    the fp64 oracle on every row, and equal to the matching rows of a full causal
+    call when the chunk is the sequence tail."""
+    import blackwell_b200 as bw
+    B, Hq, Hkv = 2, 4, 2
+    q = seeded_bf16((B, Hq, Sq, D), 71)
+    k, v = seeded_bf16((B, Hkv, Skv, D), 72), seeded_bf16((B, Hkv, Skv, D), 73)
+    o, lse = bw.gqa_causal_offset_fwd(q.cuda(), k.cuda(), v.cuda(), q_offset)
+    assert bw.stream_status() == 0
+    rows = np.array([[b, h, i] for b in range(B) for h in range(Hq) for i in range(Sq)])
+    ro, rl = orc.fp64_rows(q, k, v, 1 / math.sqrt(D), True, rows, q_offset=q_offset)
+    oc, lc = o.float().cpu().numpy().reshape(-1, D), lse.cpu().numpy().reshape(-1)
+    assert np.abs(oc - ro).max() <= O_TOL
+    assert np.abs(lc - rl).max() <= LSE_TOL
+    if q_offset + Sq == Skv:
+        qf = torch.cat([seeded_bf16((B, Hq, q_offset, D), 74), q], dim=2) if q_offset else q
+        fo, fl = bw.gqa_causal_fwd(qf.cuda(), k.cuda(), v.cuda())
+        assert (fo[:, :, q_offset:].float() - o.float()).abs().max().item() <= 2 ** -7
+        assert (fl[:, :, q_offset:] - lse).abs().max().item() <= 1e-4
+
+
 def test_mha_fp32_golden(golden):
     """fp32 MHA (the reference's mha_v3_tc data types) against the reference's
     fp64 ground truth on its own input distribution (U[0,1) - 0.5, fp32)."""
