@@ -78,13 +78,16 @@ int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, 
   return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
 }
 
-// 2-D map over [rows, cols] bf16 (row stride = cols), box (64, 64), 128B swizzle.
-int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint32_t box_rows = 64) {
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64, box_rows};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+// 3-D map over a [rows, Hkv, D] bf16 K or V array for the decode kernels:
+// dims (64, rows, Hkv * D / 64), strides (Hkv * D * 2, 128) bytes, box
+// (64, box_rows, D / 64): one load = both 64-column panels of box_rows rows of
+// one KV head, written panel after panel.
+int make_map_kv3d(CUtensorMap* m, const void* base, int64_t rows, int Hkv, int D, uint32_t box_rows) {
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)Hkv * D / 64};
+  cuuint64_t strides[2] = {(cuuint64_t)Hkv * D * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, (cuuint32_t)(D / 64)};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
@@ -330,8 +333,8 @@ static int decode_impl(const void* Q, const void* K, const void* V, const int* k
   if (rc != BW_OK) return rc;
 
   bw::DecodeMaps maps;
-  if (make_map_2d(&maps.k, K, total_tokens, (int64_t)Hkv * D) != BW_OK) return BW_ERR_CUDA;
-  if (make_map_2d(&maps.v, V, total_tokens, (int64_t)Hkv * D) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_kv3d(&maps.k, K, total_tokens, Hkv, D, 64) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_kv3d(&maps.v, V, total_tokens, Hkv, D, 64) != BW_OK) return BW_ERR_CUDA;
 
   const int64_t parts = decode_max_parts(B, Hkv, total_tokens, chunk);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -426,8 +429,8 @@ int bw_gqa_decode_paged(const void* Q, const void* K_cache, const void* V_cache,
   if (rc != BW_OK) return rc;
   const uint32_t box_rows = page_size < 64 ? (uint32_t)page_size : 64u;
   bw::DecodeMaps maps;
-  if (make_map_2d(&maps.k, K_cache, rows, (int64_t)Hkv * D, box_rows) != BW_OK) return BW_ERR_CUDA;
-  if (make_map_2d(&maps.v, V_cache, rows, (int64_t)Hkv * D, box_rows) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_kv3d(&maps.k, K_cache, rows, Hkv, D, box_rows) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_kv3d(&maps.v, V_cache, rows, Hkv, D, box_rows) != BW_OK) return BW_ERR_CUDA;
 
   const int64_t parts = decode_max_parts(B, Hkv, bound, chunk);
   uint8_t* ws = static_cast<uint8_t*>(workspace);

@@ -32,7 +32,6 @@ constexpr int kBtCacheEntries = 160;   // page indices cached per work item (chu
 
 template <int D>
 struct DecCfg {
-  static constexpr int kPanel = kTok * 128;                // 64 tokens x 64 dims bf16
   static constexpr int kHalf = kTok * D * 2;               // K (or V) part of a stage
   static constexpr int kStage = 2 * kHalf;
   static constexpr int kAcc = kStages * kStage;            // fp32 [16][D] accumulator
@@ -179,15 +178,13 @@ __global__ void __launch_bounds__(kThreads)
           mbar_arrive_expect_tx(&bars.full[s], C::kStage);
           uint8_t* dst = smem + s * C::kStage;
           if (bt_b == nullptr) {
-#pragma unroll
-            for (int pn = 0; pn < D / 64; ++pn) {
-              tma_load_2d(dst + pn * C::kPanel, &maps.k, &bars.full[s], it.kvh * D + pn * 64, (int)t);
-              tma_load_2d(dst + C::kHalf + pn * C::kPanel, &maps.v, &bars.full[s], it.kvh * D + pn * 64, (int)t);
-            }
+            tma_load_3d(dst, &maps.k, &bars.full[s], 0, (int)t, it.kvh * (D / 64));
+            tma_load_3d(dst + C::kHalf, &maps.v, &bars.full[s], 0, (int)t, it.kvh * (D / 64));
           } else {
             // Paged: the 64-token stage is gathered page piece by page piece
-            // (bh = min(64, page_size) rows per box).  Pieces past the end of the
-            // sequence re-read its last piece (in range; masked by the consumers).
+            // (bh = min(64, page_size) rows per box, both panels per load).
+            // Pieces past the end of the sequence re-read its last piece (in
+            // range; masked by the consumers).
             const int bh = p.page_size < kTok ? p.page_size : kTok;
             const int last = ((len_b - 1) / bh) * bh;
             for (int sub = 0; sub < kTok / bh; ++sub) {
@@ -196,12 +193,9 @@ __global__ void __launch_bounds__(kThreads)
               const int pi = tok / p.page_size;
               const int page = cached ? bt_cache[pi - pg0] : bt_b[pi];
               const int row = page * p.page_size + tok % p.page_size;
-#pragma unroll
-              for (int pn = 0; pn < D / 64; ++pn) {
-                tma_load_2d(dst + pn * C::kPanel + sub * bh * 128, &maps.k, &bars.full[s], it.kvh * D + pn * 64, row);
-                tma_load_2d(dst + C::kHalf + pn * C::kPanel + sub * bh * 128, &maps.v, &bars.full[s],
-                            it.kvh * D + pn * 64, row);
-              }
+              const int off = sub * (D / 64) * bh * 128;
+              tma_load_3d(dst + off, &maps.k, &bars.full[s], 0, row, it.kvh * (D / 64));
+              tma_load_3d(dst + C::kHalf + off, &maps.v, &bars.full[s], 0, row, it.kvh * (D / 64));
             }
           }
         }
@@ -222,6 +216,19 @@ __global__ void __launch_bounds__(kThreads)
   const int g = lane >> 2, q4 = lane & 3;
   const float cl2 = p.scale_log2;
   uint32_t n = 0;
+  // Shared-memory layout of a K (or V) stage: pieces of bh rows (bh = 64, or
+  // the page size below 64), each piece holding its D / 64 panels one after
+  // the other (bh x 128 bytes, 128-byte swizzled): token tl, 16-byte chunk c
+  // sits at piece(tl) + (c / 8) * bh * 128 + (tl % bh) * 128 + ((c % 8) ^ (tl % 8)) * 16.
+  const int bh = (p.block_table != nullptr && p.page_size < kTok) ? p.page_size : kTok;
+  const uint32_t panel_b = (uint32_t)bh * 128;
+  auto tok_off = [&](int tl) -> uint32_t {
+    return (uint32_t)(tl / bh) * (D / 64) * panel_b + (uint32_t)(tl % bh) * 128;
+  };
+  uint32_t k_off[2], v_off;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) k_off[nt] = tok_off(warp * 16 + nt * 8 + (lane & 7));
+  v_off = tok_off(warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7));
   bool ok = true;
   for (int idx = blockIdx.x; ok && idx < total; idx += gridDim.x) {
     const DecItem it = dec_item(p, prefix, idx);
@@ -261,7 +268,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
           for (int qq = 0; qq < D / 32; ++qq) {
             const int chunk = qq * 4 + (lane >> 3);
-            const uint32_t addr = kb + (chunk >> 3) * C::kPanel + tl * 128 + (((chunk & 7) ^ (tl & 7)) << 4);
+            const uint32_t addr = kb + k_off[nt] + (chunk >> 3) * panel_b + (((chunk & 7) ^ (tl & 7)) << 4);
             uint32_t r[4];
             ldsm_x4(addr, r);
             mma_bf16_16816(sacc[nt], qa[2 * qq], r[0], r[1]);
@@ -313,7 +320,7 @@ __global__ void __launch_bounds__(kThreads)
           const int mi = lane >> 3;
           const int tl = warp * 16 + (mi & 1) * 8 + (lane & 7);
           const int chunk = 2 * e + (mi >> 1);
-          const uint32_t addr = vb + (chunk >> 3) * C::kPanel + tl * 128 + (((chunk & 7) ^ (tl & 7)) << 4);
+          const uint32_t addr = vb + v_off + (chunk >> 3) * panel_b + (((chunk & 7) ^ (tl & 7)) << 4);
           uint32_t r[4];
           ldsm_x4_t(addr, r);
           mma_bf16_16816(o[2 * e], pa, r[0], r[1]);

@@ -99,13 +99,13 @@ int bw_gqa_decode_static(const void* Q, const void* K, const void* V, const int*
   if (rc != BW_OK) return rc;
   auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(enc);
 
-  bw::DecodeMaps maps;
+  bw::DecodeMaps maps;   // the 3-D layout launch_decode expects (kernels.h)
   for (int i = 0; i < 2; ++i) {
-    cuuint64_t dims[2] = {(cuuint64_t)Hkv * D, (cuuint64_t)total_tokens};
-    cuuint64_t strides[1] = {(cuuint64_t)Hkv * D * 2};
-    cuuint32_t box[2] = {64, 64};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = encode(i == 0 ? &maps.k : &maps.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+    cuuint64_t dims[3] = {64, (cuuint64_t)total_tokens, (cuuint64_t)Hkv * D / 64};
+    cuuint64_t strides[2] = {(cuuint64_t)Hkv * D * 2, 128};
+    cuuint32_t box[3] = {64, 64, (cuuint32_t)(D / 64)};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = encode(i == 0 ? &maps.k : &maps.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
                         const_cast<void*>(i == 0 ? K : V), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -78,7 +78,11 @@ struct DecodeParams {
 };
 
 struct DecodeMaps {
-  CUtensorMap k, v;              // 2-D (Hkv*D, rows) bf16, box (64, min(64, page_size)), SWIZZLE_128B
+  // 3-D (64, rows, Hkv * D / 64) bf16 over a [rows, Hkv, D] K or V array: dim 1
+  // steps rows (stride Hkv * D * 2 bytes), dim 2 steps 64-element panels
+  // (stride 128 bytes); box (64, min(64, page_size), D / 64), SWIZZLE_128B.
+  // One load brings both panels of a piece of up to 64 rows of one KV head.
+  CUtensorMap k, v;
 };
 
 cudaError_t launch_decode(const DecodeParams& p, const DecodeMaps& maps, int num_sms, cudaStream_t stream);
