@@ -144,9 +144,9 @@ __global__ void __launch_bounds__(kThreads)
 
   if (warp == kConsumers) {
     // ------------------------------------------------------------ producer
-    // Lane 0 issues the TMA loads.  For a paged cache the whole warp first
-    // copies the item's page indices into shared memory (one coalesced load),
-    // so lane 0 never waits on the block table between loads.
+    // For a paged cache the whole warp first copies the item's page indices
+    // into shared memory (one coalesced load), so no load waits on the block
+    // table; each lane then issues the loads of one page piece of a stage.
     int* bt_cache = reinterpret_cast<int*>(smem + C::kBtCache);
     if (lane == 0) {
       prefetch_tmap(&maps.k);
@@ -168,35 +168,42 @@ __global__ void __launch_bounds__(kThreads)
           for (int i = pg0 + lane; i <= pg1; i += 32) bt_cache[i - pg0] = bt_b[i];
         __syncwarp();
       }
-      if (lane == 0) {
-        for (int64_t t = it.t0; t < it.t1; t += kTok, ++n) {
-          const uint32_t s = n % kStages;
-          if (!wc.wait(&bars.empty[s], ((n / kStages) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&bars.full[s], C::kStage);
-          uint8_t* dst = smem + s * C::kStage;
-          if (bt_b == nullptr) {
+      // Lane 0 waits for the slot and posts the byte count; then the loads are
+      // issued, for a paged cache one page piece per lane.
+      for (int64_t t = it.t0; t < it.t1; t += kTok, ++n) {
+        const uint32_t s = n % kStages;
+        bool got = true;
+        if (lane == 0) {
+          got = wc.wait(&bars.empty[s], ((n / kStages) & 1) ^ 1);
+          if (got) mbar_arrive_expect_tx(&bars.full[s], C::kStage);
+        }
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = smem + s * C::kStage;
+        if (bt_b == nullptr) {
+          if (lane == 0) {
             tma_load_3d(dst, &maps.k, &bars.full[s], 0, (int)t, it.kvh * (D / 64));
             tma_load_3d(dst + C::kHalf, &maps.v, &bars.full[s], 0, (int)t, it.kvh * (D / 64));
-          } else {
-            // Paged: the 64-token stage is gathered page piece by page piece
-            // (bh = min(64, page_size) rows per box, both panels per load).
-            // Pieces past the end of the sequence re-read its last piece (in
-            // range; masked by the consumers).
-            const int bh = p.page_size < kTok ? p.page_size : kTok;
+          }
+        } else {
+          // Paged: the 64-token stage is gathered page piece by page piece
+          // (bh = min(64, page_size) rows per box, both panels per load).
+          // Pieces past the end of the sequence re-read its last piece (in
+          // range; masked by the consumers).
+          const int bh = p.page_size < kTok ? p.page_size : kTok;
+          const int sub = lane;
+          if (sub < kTok / bh) {
             const int last = ((len_b - 1) / bh) * bh;
-            for (int sub = 0; sub < kTok / bh; ++sub) {
-              int tok = (int)t + sub * bh;
-              if (tok > last) tok = last;
-              const int pi = tok / p.page_size;
-              const int page = cached ? bt_cache[pi - pg0] : bt_b[pi];
-              const int row = page * p.page_size + tok % p.page_size;
-              const int off = sub * (D / 64) * bh * 128;
-              tma_load_3d(dst + off, &maps.k, &bars.full[s], 0, row, it.kvh * (D / 64));
-              tma_load_3d(dst + C::kHalf + off, &maps.v, &bars.full[s], 0, row, it.kvh * (D / 64));
-            }
+            int tok = (int)t + sub * bh;
+            if (tok > last) tok = last;
+            const int pi = tok / p.page_size;
+            const int page = cached ? bt_cache[pi - pg0] : bt_b[pi];
+            const int row = page * p.page_size + tok % p.page_size;
+            const int off = sub * (D / 64) * bh * 128;
+            tma_load_3d(dst + off, &maps.k, &bars.full[s], 0, row, it.kvh * (D / 64));
+            tma_load_3d(dst + C::kHalf + off, &maps.v, &bars.full[s], 0, row, it.kvh * (D / 64));
           }
         }
       }
