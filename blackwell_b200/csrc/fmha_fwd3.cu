@@ -69,8 +69,8 @@ struct L3 {
   static constexpr int kTile = kRows * D * 2;   // one 128-row bf16 tile
   static constexpr int kSub = kRows * 128;      // one 128-byte swizzle panel
   static constexpr int kPanels = D / 64;
-  static constexpr int kQ = 0;
-  static constexpr int kKV = kTile;
+  static constexpr int kQ = 0;                  // two Q slots: the next segment's tile loads during this one
+  static constexpr int kKV = 2 * kTile;
   static constexpr int kXBytes = Split<D>::N * kRows * 8;     // (m, l) exchange: [N parts][128 rows] float2
   static constexpr int kNSraw = (kSmemBudget - kKV - 512 - kXBytes) / kTile;
   static constexpr int NS = kNSraw > kMaxSlots ? kMaxSlots : kNSraw;
@@ -81,7 +81,7 @@ struct L3 {
 };
 
 struct Bars3 {
-  uint64_t q_full, q_empty, s_full[3], p_full[3], pv_done[3], o_full, o_empty, mma_done, qk_done, xch;
+  uint64_t q_full[2], q_empty[2], s_full[3], p_full[3], pv_done[3], o_full, o_empty, mma_done, qk_done, xch;
   uint64_t kv_full[kMaxSlots], kv_empty[kMaxSlots];
   uint32_t tmem_base;
   int abort_flag;
@@ -149,17 +149,31 @@ __device__ void producer3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sm
     ++ld;
     return true;
   };
+  // Q tiles run one segment ahead: the next segment's Q load is issued right
+  // after the current segment's first K tiles, into the other Q slot (freed
+  // by the previous segment's last QK^T), so it has a whole segment to land.
+  auto load_q = [&](const Item3& it, int sg) -> bool {
+    const uint32_t qs = qn & 1;
+    if (!wc.wait(&bars.q_empty[qs], ((qn >> 1) & 1) ^ 1)) return false;
+    mbar_arrive_expect_tx(&bars.q_full[qs], L::kTile);
+    const int qt = sg == 0 ? it.qt[0] : it.qt[1];
+    for (int c = 0; c < L::kPanels; ++c)
+      tma_load_4d(smem + L::kQ + qs * L::kTile + c * L::kSub, &maps.q, &bars.q_full[qs], c * 64, qt * kRows, it.h,
+                  it.b);
+    ++qn;
+    return true;
+  };
+  if (blockIdx.x < p.num_items) ok = load_q(decode_item3(p, blockIdx.x), 0);
   for (int idx = blockIdx.x; ok && idx < p.num_items; idx += gridDim.x) {
     const Item3 it = decode_item3(p, idx);
     for (int sg = 0; ok && sg < it.nseg; ++sg) {
       const int n = sg == 0 ? it.n[0] : it.n[1];
-      if (!wc.wait(&bars.q_empty, (qn & 1) ^ 1)) { ok = false; break; }
-      mbar_arrive_expect_tx(&bars.q_full, L::kTile);
-      for (int c = 0; c < L::kPanels; ++c)
-        tma_load_4d(smem + L::kQ + c * L::kSub, &maps.q, &bars.q_full, c * 64, (sg == 0 ? it.qt[0] : it.qt[1]) * kRows, it.h, it.b);
-      ++qn;
       ok = load_kv(true, 0, it);
       if (ok && n > 1) ok = load_kv(true, 1, it);
+      if (ok) {   // the next segment's Q
+        if (sg + 1 < it.nseg) ok = load_q(it, sg + 1);
+        else if (idx + (int)gridDim.x < p.num_items) ok = load_q(decode_item3(p, idx + gridDim.x), 0);
+      }
       for (int j = 0; ok && j < n; ++j) {
         ok = load_kv(false, j, it);
         if (ok && j + 2 < n) ok = load_kv(true, j + 2, it);
@@ -171,7 +185,7 @@ __device__ void producer3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sm
       const uint32_t slot = i % NS;
       if (armed & (1u << slot)) drain_wait(&bars.kv_full[slot], (i / NS) & 1, wc.timeout_ns);
     }
-    if (qn) drain_wait(&bars.q_full, (qn - 1) & 1, wc.timeout_ns);
+    for (uint32_t i = qn > 2 ? qn - 2 : 0; i < qn; ++i) drain_wait(&bars.q_full[i & 1], (i >> 1) & 1, wc.timeout_ns);
   }
 }
 
@@ -215,8 +229,10 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
     const Item3 it = decode_item3(p, idx);
     for (int sg = 0; ok && sg < it.nseg; ++sg) {
       const int n = sg == 0 ? it.n[0] : it.n[1];
-      if (!wc.wait(&bars.q_full, qn & 1)) { ok = false; break; }
+      const uint32_t qs = qn & 1;
+      if (!wc.wait(&bars.q_full[qs], (qn >> 1) & 1)) { ok = false; break; }
       ++qn;
+      const uint32_t qa = q_lo + qs * (uint32_t)(L::kTile / 16);
       for (int j = 0; j < n; ++j) {
         constexpr uint32_t NB = Split<D>::NB;
         const uint32_t g = tc + j, buf = g % NB;
@@ -230,12 +246,12 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t off = ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
-          mma_ss_lh(tmem + buf * 128, q_lo + off, HI, ka + off, HI, IDESC_QK, ks > 0);
+          mma_ss_lh(tmem + buf * 128, qa + off, HI, ka + off, HI, IDESC_QK, ks > 0);
         }
         BW_TRACE_AT(true, 24, g);
         tc_commit(&bars.s_full[buf]);
         tc_commit(&bars.kv_empty[e % NS]);
-        if (j == n - 1) tc_commit(&bars.q_empty);
+        if (j == n - 1) tc_commit(&bars.q_empty[qs]);
       }
       if (!ok) break;
       tc += n;
@@ -491,8 +507,10 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
   constexpr int kProducer = kSoftWarps, kPvIssuer = kSoftWarps + 1;
 
   if (tid == 0) {
-    mbar_init(&bars.q_full, 1);
-    mbar_init(&bars.q_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars.q_full[b], 1);
+      mbar_init(&bars.q_empty[b], 1);
+    }
     for (int b = 0; b < Split<D>::NB; ++b) {
       mbar_init(&bars.s_full[b], 1);
       mbar_init(&bars.p_full[b], 128 * Split<D>::N);
