@@ -1,4 +1,4 @@
-"""Builds the reference's own split-length GQA kernel program (TEST INFRASTRUCTURE ONLY).
+"""Builds the reference's own SM120 attention programs (TEST INFRASTRUCTURE ONLY).
 
 The reference's `gqa_split` path is `launch_gqa_v1` in
 src/SM120/attention/adhitya_GQA.cu:199-213 (kernel :63-188, harness main()
@@ -13,6 +13,13 @@ times the kernel with the reference's own harness (25 warm-ups, 100 timed
 runs, 256 MiB L2 flush per run).  ``tests/test_reference_kernel_gpu.py``
 uses it as a cross-check and a timing comparator.
 
+Likewise the reference's fp32 MHA program (src/SM120/attention/MHA_sm120.cu:
+`mha_v3_tc`, 3xTF32 split, :64-170, launch and main() :289-370) goes to
+``oracle/_ref/mha_sm120``, with its data directory (a compile-time macro,
+MHA_DATA_DIR) set to ``data`` relative to its working directory; main() runs
+B=16, H=12, S=1024, D=64, reports the precision of its output and of the
+files' "SDPA" output against the files' fp64 output, and times the kernel.
+
 The reference's tcgen05 kernels (src/SM103) cannot be built here: nvcc 12.9
 rejects their > 48 KB static shared memory.
 """
@@ -24,6 +31,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "adhitya_gqa"
+OUT_MHA = HERE / "_ref" / "mha_sm120"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
@@ -32,23 +40,32 @@ def default_reference_root() -> Path:
     return HERE.parent.parent / "reference"
 
 
-def build(reference_root: Path | None = None, verbose: bool = False) -> Path | None:
-    """Compile the reference program; returns its path, or None when the
-    reference tree is not present (the GPU box only uses the prebuilt file)."""
-    root = Path(reference_root) if reference_root else default_reference_root()
-    src = root / "src" / "SM120" / "attention" / "adhitya_GQA.cu"
-    inc = root / "include"
-    if not src.is_file() or not (inc / "utils" / "kernelBench.cuh").is_file():
-        return None
-    if OUT.exists() and OUT.stat().st_mtime >= src.stat().st_mtime:
-        return OUT
-    OUT.parent.mkdir(exist_ok=True)
-    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", f"-I{inc}", str(src),
-           "-o", str(OUT)]
+def _compile(src: Path, inc: Path, out: Path, extra: list[str], verbose: bool) -> Path:
+    if out.exists() and out.stat().st_mtime >= src.stat().st_mtime:
+        return out
+    out.parent.mkdir(exist_ok=True)
+    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", f"-I{inc}", *extra, str(src),
+           "-o", str(out)]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    return OUT
+    return out
+
+
+def build(reference_root: Path | None = None, verbose: bool = False) -> list[Path]:
+    """Compile the reference programs; returns their paths (empty when the
+    reference tree is not present: the GPU box only uses the prebuilt files)."""
+    root = Path(reference_root) if reference_root else default_reference_root()
+    att = root / "src" / "SM120" / "attention"
+    inc = root / "include"
+    if not (inc / "utils" / "kernelBench.cuh").is_file():
+        return []
+    built = []
+    if (att / "adhitya_GQA.cu").is_file():
+        built.append(_compile(att / "adhitya_GQA.cu", inc, OUT, [], verbose))
+    if (att / "MHA_sm120.cu").is_file():
+        built.append(_compile(att / "MHA_sm120.cu", inc, OUT_MHA, ["-DMHA_DATA_DIR=data"], verbose))
+    return built
 
 
 if __name__ == "__main__":

@@ -65,3 +65,67 @@ def test_reference_split_kernel_agrees(tmp_path):
           f"bw_gqa_split_fwd median {ours:.4f} ms ({flops / ours / 1e9:.1f} TFLOP/s); "
           f"speed-up {ref_ms / ours:.1f}x")
     assert ours < ref_ms
+
+
+REF_MHA = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "mha_sm120"
+
+
+def _max_abs(out, label):
+    line = next(ln for ln in out.splitlines() if label in ln)
+    return float(re.search(r"max_abs=([\d.eE+-]+)", line).group(1))
+
+
+@pytest.mark.skipif(not REF_MHA.exists(), reason="reference program not built (oracle/build_ref.py)")
+def test_reference_mha_fp32_kernel_agrees(tmp_path):
+    """The reference's fp32 MHA kernel (mha_v3_tc, 3xTF32) at its program's
+    shape (B=16, H=12, S=1024, D=64) on inputs U[0,1) - 0.5, with the files'
+    "SDPA" output = bw_mha_fwd_f32 and their fp64 output = the oracle: the
+    reference kernel must sit on the oracle (this pins the oracle with the
+    reference's own GPU code), and ours within 2e-3 of both."""
+    import blackwell_b200 as bw
+    from oracle import attention_oracle as orc
+
+    B, H, S, D = 16, 12, 1024, 64
+    g = torch.Generator().manual_seed(11)
+    q, k, v = (torch.rand(B, H, S, D, generator=g) - 0.5 for _ in range(3))
+    scale = 1.0 / math.sqrt(D)
+    o, _ = bw.mha_fwd_f32(q.cuda(), k.cuda(), v.cuda(), scale)
+    assert bw.stream_status() == 0
+    # fp64 ground truth, batched over heads (same arithmetic as the oracle's
+    # per-head restatement of baseline_mha.py:28-33)
+    q64, k64, v64 = (t.double() for t in (q, k, v))
+    ref64 = torch.softmax(q64 @ k64.transpose(-1, -2) * scale, dim=-1) @ v64
+    h0 = orc.fp64_attention(q[:1, :1], k[:1, :1], v[:1, :1], scale)
+    assert np.abs(h0 - ref64[:1, :1].numpy()).max() < 1e-6      # same as the oracle
+    data = tmp_path / "data"
+    data.mkdir()
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", o.cpu()), ("out_fp64", ref64)):
+        t.float().numpy().astype(np.float32).tofile(data / f"mha_{name}.bin")
+    res = subprocess.run([str(REF_MHA)], cwd=tmp_path, capture_output=True, text=True, timeout=600)
+    out = res.stdout
+    print(out[-1500:])
+    assert res.returncode == 0, res.stderr[-2000:]
+    ref_vs_fp64 = _max_abs(out, "mha_v3_tc    vs  fp64")
+    ours_vs_fp64 = _max_abs(out, "torch.SDPA   vs  fp64")     # the files' "SDPA" slot holds our output
+    ref_vs_ours = _max_abs(out, "mha_v3_tc    vs  SDPA")
+    assert ref_vs_fp64 <= 1e-5, ref_vs_fp64
+    assert ours_vs_fp64 <= 2e-3 and ref_vs_ours <= 2e-3, (ours_vs_fp64, ref_vs_ours)
+    ref_ms = float(re.search(r"Median Time:\s+([\d.]+)", out).group(1))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    times = []
+    for i in range(30):
+        flush.zero_()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record()
+        bw.mha_fwd_f32(qd, kd, vd, scale)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 5:
+            times.append(a.elapsed_time(b))
+    ours = statistics.median(times)
+    flops = 4.0 * B * H * S * S * D
+    print(f"reference mha_v3_tc median {ref_ms:.3f} ms ({flops / ref_ms / 1e9:.1f} TFLOP/s); "
+          f"bw_mha_fwd_f32 median {ours:.4f} ms ({flops / ours / 1e9:.1f} TFLOP/s); speed-up {ref_ms / ours:.1f}x; "
+          f"max-abs vs fp64: reference {ref_vs_fp64:.2e}, ours {ours_vs_fp64:.2e}")
+    assert ours < ref_ms
