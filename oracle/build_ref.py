@@ -13,6 +13,11 @@ times the kernel with the reference's own harness (25 warm-ups, 100 timed
 runs, 256 MiB L2 flush per run).  ``tests/test_reference_kernel_gpu.py``
 uses it as a cross-check and a timing comparator.
 
+The reference's non-causal GQA program (src/SM120/attention/GQA_sm120.cu:
+`gqa_v1` two-pass :58-184 and `gqa_v2` online softmax :187-345, main()
+:383-518) goes to ``oracle/_ref/gqa_sm120``: B=16, Hq=12, Hkv=4, S=4096,
+D=64, checked against ``data/gqa_*.bin`` the same way.
+
 Likewise the reference's fp32 MHA program (src/SM120/attention/MHA_sm120.cu:
 `mha_v3_tc`, 3xTF32 split, :64-170, launch and main() :289-370) goes to
 ``oracle/_ref/mha_sm120``, with its data directory (a compile-time macro,
@@ -32,6 +37,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "adhitya_gqa"
 OUT_MHA = HERE / "_ref" / "mha_sm120"
+OUT_GQA = HERE / "_ref" / "gqa_sm120"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
@@ -63,6 +69,8 @@ def build(reference_root: Path | None = None, verbose: bool = False) -> list[Pat
     built = []
     if (att / "adhitya_GQA.cu").is_file():
         built.append(_compile(att / "adhitya_GQA.cu", inc, OUT, [], verbose))
+    if (att / "GQA_sm120.cu").is_file():
+        built.append(_compile(att / "GQA_sm120.cu", inc, OUT_GQA, [], verbose))
     if (att / "MHA_sm120.cu").is_file():
         built.append(_compile(att / "MHA_sm120.cu", inc, OUT_MHA, ["-DMHA_DATA_DIR=data"], verbose))
     return built

@@ -67,6 +67,57 @@ def test_reference_split_kernel_agrees(tmp_path):
     assert ours < ref_ms
 
 
+REF_GQA = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "gqa_sm120"
+
+
+@pytest.mark.skipif(not REF_GQA.exists(), reason="reference program not built (oracle/build_ref.py)")
+def test_reference_gqa_kernels_agree(tmp_path):
+    """The reference's non-causal GQA kernels (gqa_v1 two-pass, gqa_v2 online
+    softmax; GQA_sm120.cu) at their program's shape (B=16, Hq=12, Hkv=4,
+    S=4096, D=64) checked by the program's own checkResult against
+    bw_gqa_fwd's O and LSE, and timed against it."""
+    import blackwell_b200 as bw
+
+    B, Hq, Hkv, S, D = 16, 12, 4, 4096, 64
+    g = torch.Generator().manual_seed(13)
+    q = torch.randn(B, Hq, S, D, generator=g).bfloat16()
+    k = torch.randn(B, Hkv, S, D, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, S, D, generator=g).bfloat16()
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    scale = 1.0 / math.sqrt(D)
+    o, lse = bw.gqa_fwd(qd, kd, vd, scale)
+    assert bw.stream_status() == 0
+    data = tmp_path / "data"
+    data.mkdir()
+    for name, t in (("q", q), ("k", k), ("v", v), ("o", o.cpu()), ("lse", lse.cpu())):
+        t.float().numpy().astype(np.float32).tofile(data / f"gqa_{name}.bin")
+    res = subprocess.run([str(REF_GQA)], cwd=tmp_path, capture_output=True, text=True, timeout=900)
+    out = res.stdout
+    print(out[-2500:])
+    assert res.returncode == 0, res.stderr[-2000:]
+    assert "Loaded PyTorch reference" in out
+    assert out.count("Values match!") == 4, out[-2500:]      # O and LSE for V1 and V2
+    ref_ms = [float(x) for x in re.findall(r"Median Time:\s+([\d.]+)", out)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    times = []
+    for i in range(30):
+        flush.zero_()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record()
+        bw.gqa_fwd(qd, kd, vd, scale, out=o, lse=lse)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 5:
+            times.append(a.elapsed_time(b))
+    ours = statistics.median(times)
+    flops = 4.0 * B * Hq * S * S * D
+    print(f"reference gqa_v1 / gqa_v2 median {ref_ms[0]:.3f} / {ref_ms[1]:.3f} ms "
+          f"({flops / ref_ms[0] / 1e9:.1f} / {flops / ref_ms[1] / 1e9:.1f} TFLOP/s); "
+          f"bw_gqa_fwd median {ours:.4f} ms ({flops / ours / 1e9:.1f} TFLOP/s); "
+          f"speed-up {min(ref_ms) / ours:.1f}x over the faster")
+    assert ours < min(ref_ms)
+
+
 REF_MHA = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "mha_sm120"
 
 
