@@ -2,7 +2,8 @@
 
     python -m blackwell_b200.build        # -> blackwell_b200/libbw_attn.so
 
-Every .cu under csrc/ is compiled with
+It also links the C++ harness ``bw_harness`` (harness/bw_harness.cpp) against
+the library.  Every .cu under csrc/ is compiled with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`` and linked into one
 shared library with the CUDA runtime linked statically (no torch types cross
 the boundary; the library only depends on the driver at run time).
@@ -18,6 +19,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT = HERE / "libbw_attn.so"
+HARNESS = HERE / "bw_harness"
+HARNESS_SRC = HERE / "harness" / "bw_harness.cpp"
 BUILD = HERE / "_build"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
@@ -33,10 +36,10 @@ def _deps():
 
 
 def up_to_date() -> bool:
-    if not OUT.exists():
+    if not OUT.exists() or not HARNESS.exists():
         return False
-    t = OUT.stat().st_mtime
-    return all(p.stat().st_mtime <= t for p in _deps())
+    t = min(OUT.stat().st_mtime, HARNESS.stat().st_mtime)
+    return all(p.stat().st_mtime <= t for p in _deps() + [HARNESS_SRC])
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -58,7 +61,19 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(tmp), *map(str, objs)]
     subprocess.run(cmd, check=True)
     os.replace(tmp, OUT)
+    build_harness(verbose)
     return OUT
+
+
+def build_harness(verbose: bool = False) -> Path:
+    """The C++ harness (reference-style main over the C ABI), linked to the library."""
+    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-I", str(HERE.parent / "include"),
+           str(HARNESS_SRC), "-o", str(HARNESS),
+           "-L", str(HERE), "-lbw_attn", "-Xlinker", "-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    return HARNESS
 
 
 if __name__ == "__main__":
