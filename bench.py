@@ -148,6 +148,17 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def c2_config(world):
+    """The workload description both arms report (C2)."""
+    B, Hq, Hkv, S, D = (C2[k] for k in ("B", "Hq", "Hkv", "S", "D"))
+    return {"workload": "C2 causal GQA prefill (Llama-3-8B attention shape)", "entry": "bw_gqa_causal_fwd",
+            "batch_total": B * world, "batch_per_gpu": B, "seq_len": S, "heads_q": Hq, "heads_kv": Hkv,
+            "head_dim": D, "layout": "BSHD",
+            "parallelism": f"shard by batch x KV-group, {world} rank(s), no collective",
+            "l2": "256 MiB buffer written before every step, outside the event pair",
+            "flops_per_step": causal_flops(B, Hq, S, D) * world, "flop_count": "4*B*Hq*S^2*D/2"}
+
+
 # ---------------------------------------------------------------- CPU path
 class CpuReference:
     """The reference's CPU path (torch SDPA, enable_gqa, causal) on one (b, KV-group)
@@ -197,8 +208,7 @@ def run_reference(args, world, rank):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(t) / len(t),
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1), seed 42", "scaling": "weak",
-            "config": {"workload": "C2 causal GQA prefill B=4 Hq=32 Hkv=8 S=4096 D=128 BSHD",
-                       "cpu_sample": ref.sample},
+            "config": dict(c2_config(world), cpu_sample=ref.sample),
             "cpu_baseline": cpu,
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "vs_baseline": None}
@@ -460,11 +470,7 @@ def run_ours(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": per_launch_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seed 42 (+rank)",
-            "config": {"workload": "C2 causal GQA prefill (Llama-3-8B attention shape)", "model": "gqa_causal_fwd",
-                       "global_batch": B * world, "seq_len": S, "heads_q": Hq, "heads_kv": Hkv, "head_dim": D,
-                       "layout": "BSHD", "parallelism": f"shard by batch x KV-group, {world} rank(s), no collective",
-                       "l2": "256 MiB buffer written before every step, outside the event pair",
-                       "flops_per_step": flops, "flop_count": "4*B*Hq*S^2*D/2"},
+            "config": c2_config(world),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": achieved / peaks["bf16_tflops"], "peak_kind": f"{peak_kind} bf16 burst",
                          "traffic": profile_traffic("fmha_fwd_c2_launches.md")},
