@@ -12,14 +12,20 @@ from tests._util import seeded_bf16
 pytestmark = pytest.mark.gpu
 
 
-def test_withheld_tile_reports_timeout_and_recovers():
+@pytest.mark.parametrize("kernel,D", [(0, 64), (0, 128), (1, 128), (3, 64)],
+                         ids=["auto_d64", "auto_d128", "k1_d128", "k3_d64"])
+def test_withheld_tile_reports_timeout_and_recovers(kernel, D):
+    """Each prefill kernel (kernel 3 is the D = 128 default, kernel 1 the D = 64
+    one): the withheld K tile makes every role's bounded wait expire."""
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
-    q = seeded_bf16((1, 2, 256, 64), 1).cuda()
-    k = seeded_bf16((1, 2, 256, 64), 2).cuda()
-    v = seeded_bf16((1, 2, 256, 64), 3).cuda()
+    q = seeded_bf16((1, 2, 256, D), 1).cuda()
+    k = seeded_bf16((1, 2, 256, D), 2).cuda()
+    v = seeded_bf16((1, 2, 256, D), 3).cuda()
     old_t = bw.get_option(_ffi.BW_OPT_TIMEOUT_NS)
+    old_k = bw.get_option(_ffi.BW_OPT_PREFILL_KERNEL)
     try:
+        bw.set_option(_ffi.BW_OPT_PREFILL_KERNEL, kernel)
         bw.set_option(_ffi.BW_OPT_TIMEOUT_NS, 50_000_000)   # 50 ms
         bw.set_option(_ffi.BW_OPT_DEBUG_FLAGS, 1)
         bw.mha_fwd(q, k, v)
@@ -27,6 +33,7 @@ def test_withheld_tile_reports_timeout_and_recovers():
     finally:
         bw.set_option(_ffi.BW_OPT_DEBUG_FLAGS, 0)
         bw.set_option(_ffi.BW_OPT_TIMEOUT_NS, old_t)
+        bw.set_option(_ffi.BW_OPT_PREFILL_KERNEL, old_k)
     assert bw.stream_status() == 0
     o, lse = bw.mha_fwd(q, k, v)
     assert bw.stream_status() == 0
