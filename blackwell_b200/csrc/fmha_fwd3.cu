@@ -423,14 +423,18 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.p_full[buf]);
+      // one arrival per warp: the warp's TMEM stores are complete (wait::st +
+      // fence above) and ordered before lane 0's arrival by __syncwarp
+      __syncwarp();
+      if ((t & 31) == 0) mbar_arrive(&bars.p_full[buf]);
       BW_TRACE_AT(t == 0, 3, g);
       BW_TRACE_AT(t == 128, 5, g);
       BW_TRACE_AT((t & 31) == 0 && t < 256, 10 + (t >> 5), g);
     }
     // merge the parts of the row: exchange (m, l) through shared memory
     xch[part * kRows + rl] = make_float2(m_run, l_run);
-    mbar_arrive(&bars.xch);
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&bars.xch);
     if (!wc.wait(&bars.xch, itn & 1)) return;
     float mp[N], lp[N];
 #pragma unroll
@@ -477,7 +481,8 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
     }
     // O has been read: the next item's first PV may overwrite it
     tc_fence_before();
-    mbar_arrive(&bars.o_empty);
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&bars.o_empty);
     if (row < p.Sq) {
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.O) + it.b * p.o_sb + it.h * p.o_sh +
                                             (int64_t)row * p.o_ss + part * DC);
@@ -513,13 +518,13 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
     }
     for (int b = 0; b < Split<D>::NB; ++b) {
       mbar_init(&bars.s_full[b], 1);
-      mbar_init(&bars.p_full[b], 128 * Split<D>::N);
+      mbar_init(&bars.p_full[b], 4 * Split<D>::N);   // one arrival per softmax warp
     }
     for (int b = 0; b < Split<D>::NB; ++b) mbar_init(&bars.pv_done[b], 1);
     mbar_init(&bars.qk_done, 1);
     mbar_init(&bars.o_full, 1);
-    mbar_init(&bars.o_empty, 128 * Split<D>::N);
-    mbar_init(&bars.xch, 128 * Split<D>::N);
+    mbar_init(&bars.o_empty, 4 * Split<D>::N);
+    mbar_init(&bars.xch, 4 * Split<D>::N);
     mbar_init(&bars.mma_done, 1);
     for (int s = 0; s < L::NS; ++s) {
       mbar_init(&bars.kv_full[s], 1);
