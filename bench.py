@@ -149,7 +149,7 @@ def max_over_ranks(x, world):
 
 
 def c2_config(world):
-    """The workload description both arms report (C2)."""
+    """The workload description both arms report (the C2 configuration)."""
     B, Hq, Hkv, S, D = (C2[k] for k in ("B", "Hq", "Hkv", "S", "D"))
     return {"workload": "C2 causal GQA prefill (Llama-3-8B attention shape)", "entry": "bw_gqa_causal_fwd",
             "batch_total": B * world, "batch_per_gpu": B, "seq_len": S, "heads_q": Hq, "heads_kv": Hkv,

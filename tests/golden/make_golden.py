@@ -125,7 +125,8 @@ def case_decode(mod, name, B, Hq, Hkv, D, lens):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=str(Path(__file__).resolve().parents[3] / "reference"),
+                    help="the reference checkout (default: next to this repository)")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref / "base"))
