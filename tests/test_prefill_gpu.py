@@ -263,3 +263,33 @@ def test_mha_fp32_shapes(S):
     ro, rl = orc.fp64_reference(q, k, v, 1 / math.sqrt(D))
     assert np.abs(o.cpu().numpy() - ro).max() <= O_TOL
     assert np.abs(lse.cpu().numpy() - rl).max() <= 5e-3  # TF32 logits
+
+
+@pytest.mark.parametrize("kernel", [3, 1, 2])
+@pytest.mark.parametrize("q_scale,causal", [(12.0, True), (12.0, False), (0.02, True)])
+def test_logit_range_stress(kernel, q_scale, causal):
+    """Large logits (q scaled up: the running max moves by far more than the
+    lazy-rescale threshold, and the two halves of a row in kernel 3 end with
+    very different maxima) and nearly flat ones, against fp64 rows."""
+    import blackwell_b200 as bw
+    from blackwell_b200 import _ffi
+    B, Hq, Hkv, S, D = 1, 4, 2, 640, 128
+    g = torch.Generator().manual_seed(int(q_scale * 10) + causal)
+    # keys with a growing trend so that later tiles keep raising the row max
+    q = (torch.randn(B, Hq, S, D, generator=g) * q_scale / math.sqrt(D)).bfloat16()
+    k = (torch.randn(B, Hkv, S, D, generator=g) + torch.linspace(0, 3, S)[None, None, :, None]).bfloat16()
+    v = torch.randn(B, Hkv, S, D, generator=g).bfloat16()
+    old = bw.get_option(_ffi.BW_OPT_PREFILL_KERNEL)
+    try:
+        bw.set_option(_ffi.BW_OPT_PREFILL_KERNEL, kernel)
+        o, lse = bw.gqa_split_fwd(q.cuda(), k.cuda(), v.cuda(), 1 / math.sqrt(D), causal=causal)
+        assert bw.stream_status() == 0
+    finally:
+        bw.set_option(_ffi.BW_OPT_PREFILL_KERNEL, old)
+    rows = np.array([[0, h, i] for h in range(Hq) for i in range(0, S, 7)])
+    ro, rl = orc.fp64_rows(q, k, v, 1 / math.sqrt(D), causal, rows)
+    oc = o.float().cpu().numpy()[0][rows[:, 1], rows[:, 2]]
+    lc = lse.cpu().numpy()[0][rows[:, 1], rows[:, 2]]
+    assert np.isfinite(oc).all() and np.isfinite(lc).all()
+    assert np.abs(oc - ro).max() <= O_TOL
+    assert np.abs(lc - rl).max() <= LSE_TOL * max(1.0, np.abs(rl).max() / 100)
