@@ -99,14 +99,15 @@ def test_decode_partial_pieces_merge(pieces):
     assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL
 
 
-@pytest.mark.parametrize("page_size", [8, 16, 64, 128, 256])
-def test_decode_paged(page_size):
+@pytest.mark.parametrize("page_size,D", [(8, 128), (16, 128), (32, 128), (64, 128), (128, 128), (256, 128),
+                                         (16, 64), (64, 64)])
+def test_decode_paged(page_size, D):
     """Paged KV cache: pages in a random physical order, unused block-table
     entries set to -1, partial last pages; against the oracle on the gathered
     contiguous keys."""
     import blackwell_b200 as bw
     rng = np.random.default_rng(page_size)
-    B, Hq, Hkv, D = 4, 32, 4, 128
+    B, Hq, Hkv = 4, 32, 4
     lens = np.array([1, page_size + 3, 1100, 2 * page_size])
     pages_per = (lens + page_size - 1) // page_size
     max_pages = int(pages_per.max()) + 2
