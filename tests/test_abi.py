@@ -106,3 +106,41 @@ def test_package_exports():
                  "stream_status", "set_option", "get_option", "shard_plan", "decode_workspace_size",
                  "attention_from_host", "gqa_causal_offset_fwd", "host_workspace_size"]:
         assert callable(getattr(bw, name)), name
+
+
+def test_new_entry_points_validate_without_gpu():
+    """The host-buffer call and the chunked-prefill call reject bad arguments
+    before touching the device."""
+    lib = _ffi.lib()
+    p = ctypes.c_void_p(0x100000)
+    ws = ctypes.c_void_p(0x200000)   # 256-byte aligned
+    need = lib.bw_attn_fwd_host_workspace_size(1, 8, 2, 256, 128)
+    a256 = lambda x: (x + 255) // 256 * 256
+    assert need == 2 * a256(8 * 256 * 128 * 2) + 2 * a256(2 * 256 * 128 * 2) + a256(8 * 256 * 4)
+    assert lib.bw_attn_fwd_host_workspace_size(0, 8, 2, 256, 128) == 0
+    host = lambda **kw: lib.bw_attn_fwd_host(kw.get("q", p), p, p, p, None, 1, kw.get("hq", 8), 2, 256,
+                                             kw.get("d", 128), 0.1, 1, kw.get("layout", _ffi.BW_LAYOUT_BSHD), 4,
+                                             kw.get("ws", ws), kw.get("nbytes", need), None)
+    assert host(q=None) == _ffi.BW_ERR_NULL
+    assert host(ws=None) == _ffi.BW_ERR_NULL
+    assert host(d=96) == _ffi.BW_ERR_SHAPE
+    assert host(hq=7) == _ffi.BW_ERR_SHAPE
+    assert host(layout=5) == _ffi.BW_ERR_SHAPE
+    assert host(nbytes=need - 1) == _ffi.BW_ERR_WORKSPACE
+    assert host(ws=ctypes.c_void_p(0x200010)) == _ffi.BW_ERR_ALIGN
+    off = lambda q_offset, sq=128: lib.bw_gqa_causal_offset_fwd(p, p, p, p, None, 1, 8, 2, sq, 512, 4, 128, 0.1,
+                                                                q_offset, None, None)
+    assert off(-1) == _ffi.BW_ERR_SHAPE
+    assert off(1 << 30) == _ffi.BW_ERR_SHAPE
+    assert off(0, sq=0) == _ffi.BW_ERR_SHAPE
+
+
+def test_prefill_kernel_option_values():
+    lib = _ffi.lib()
+    old = lib.bw_get_option(_ffi.BW_OPT_PREFILL_KERNEL)
+    assert old == 0                                   # default: chosen by head dimension
+    for v in (0, 1, 2, 3):
+        assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == 0
+    for v in (-1, 4):
+        assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == _ffi.BW_ERR_SHAPE
+    lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, old)
