@@ -350,6 +350,25 @@ def bench_fused(shape, flush, steps, warmup):
     return {"ms": t, "TFLOP/s": causal_flops(B, Hq, S, D) / t / 1e9}
 
 
+def bench_norm_rope(flush, steps, warmup):
+    """QK-norm + RoPE (NeoX) of the C2 query tensor [4, 32, 4096, 128] bf16, gamma
+    present: one streaming pass, 2 x 128 MiB of traffic."""
+    import blackwell_b200 as bw
+    B, H, S, D = 4, 32, 4096, 128
+    g = torch.Generator(device="cuda").manual_seed(42)
+    q = torch.randn(B, H, S, D, generator=g, device="cuda").bfloat16()
+    half = D // 2
+    inv = 10000.0 ** (-torch.arange(half, dtype=torch.float64, device="cuda") * 2.0 / D)
+    ang = torch.arange(S, dtype=torch.float64, device="cuda")[:, None] * inv[None]
+    cache = torch.cat([ang.cos(), ang.sin()], 1).float().contiguous()
+    gamma = 1 + 0.1 * torch.randn(D, generator=g, device="cuda")
+    out = torch.empty_like(q)
+    ms = time_steps(lambda: bw.qk_norm_rope(q, cache, gamma, out=out), steps, warmup, flush, 1)
+    assert bw.stream_status() == 0
+    t = statistics.median(ms)
+    return {"ms": t, "GB/s": 2 * q.numel() * 2 / t / 1e6}
+
+
 def bench_c5(world, rank, steps, warmup):
     """C5: causal GQA B=1, Hq=64, Hkv=8, S=131072, D=128, one or more KV-head groups
     per rank (8 groups sharded over the ranks, no exchange).  Each rank holds only
@@ -495,6 +514,8 @@ def run_single(args):
         r = bench_prefill(*shapes[args.workload], flush, args.steps, args.warmup)
     elif args.workload == "c4paged16":
         r = bench_decode_paged(flush, args.steps, args.warmup, page_size=16)
+    elif args.workload == "normrope":
+        r = bench_norm_rope(flush, args.steps, args.warmup)
     else:
         r = bench_decode(flush, args.steps, args.warmup, len_div=8 if args.workload == "c4small" else 1)
     print(json.dumps({"workload": args.workload, **r}), flush=True)
@@ -511,7 +532,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="short run for profiler captures: no secondary configs, no CPU baseline")
-    ap.add_argument("--workload", choices=["c2", "c3d64", "c3d128", "c4", "c4small", "c4paged16", "refshape"],
+    ap.add_argument("--workload", choices=["c2", "c3d64", "c3d128", "c4", "c4small", "c4paged16", "refshape",
+                                           "normrope"],
                     default=None,
                     help="profiler aid: run only this workload's kernel and print its timing")
     args = ap.parse_args()

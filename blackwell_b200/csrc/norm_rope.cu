@@ -25,7 +25,7 @@
 namespace bw {
 namespace {
 
-constexpr int kGroups = 4;       // row groups (warp-wide 512-byte loads) in flight per warp
+constexpr int kGroups = 2;       // row groups (two 16-byte loads per lane each) in flight per warp
 constexpr int kMinBlocks = 4;    // 256-thread blocks per SM (64 registers per thread)
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
@@ -37,18 +37,22 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 
 template <int D, bool NEOX>
 __global__ void __launch_bounds__(256, kMinBlocks) norm_rope_kernel(const NormRopeParams p) {
-  constexpr int LPR = D / 8;           // lanes per row
+  constexpr int NCH = D / 8;           // 16-byte chunks per row
+  constexpr int LPR = NCH / 2;         // lanes per row: two chunks per lane
   constexpr int RPI = 32 / LPR;        // rows per warp instruction
   constexpr int RPW = RPI * kGroups;   // rows per warp iteration
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;          // lane within its row
-  const int e0 = sub * 8;              // first element held
+  // NeoX: chunks sub and sub + NCH/2 (each element's rotation partner is in the
+  // same lane); interleaved: chunks 2 sub, 2 sub + 1 (pairs inside a chunk).
+  const int c0 = NEOX ? sub : 2 * sub, c1 = NEOX ? sub + NCH / 2 : 2 * sub + 1;
+  const int ci = 8 * sub;              // first cos / sin index this lane uses (8 of them)
   const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
   const uint32_t rows = (uint32_t)p.B * p.H * p.S;   // < 2^31, checked by the caller
 
   for (uint32_t base = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW; base < rows;
        base += warps_total * RPW) {
-    uint4 raw[kGroups];
+    uint4 raw[kGroups][2];
     int64_t out_off[kGroups];
     int pos[kGroups];
     uint32_t rs_idx[kGroups];  // [B, H, S] index of the row (rstd output)
@@ -70,75 +74,71 @@ __global__ void __launch_bounds__(256, kMinBlocks) norm_rope_kernel(const NormRo
           if (++s == p.S) { s = 0; ++b; }
         }
       }
-      raw[u] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.in) + b * p.in_sb +
-                                               h * p.in_sh + (int64_t)s * p.in_ss + e0);
-      out_off[u] = b * p.out_sb + h * p.out_sh + (int64_t)s * p.out_ss + e0;
+      const __nv_bfloat16* src =
+          reinterpret_cast<const __nv_bfloat16*>(p.in) + b * p.in_sb + h * p.in_sh + (int64_t)s * p.in_ss;
+      raw[u][0] = *reinterpret_cast<const uint4*>(src + 8 * c0);
+      raw[u][1] = *reinterpret_cast<const uint4*>(src + 8 * c1);
+      out_off[u] = b * p.out_sb + h * p.out_sh + (int64_t)s * p.out_ss;
       pos[u] = s + p.pos_offset;
       rs_idx[u] = ((uint32_t)b * p.H + h) * (uint32_t)p.S + s;
     }
 #pragma unroll
     for (int u = 0; u < kGroups; ++u) {
       const uint32_t r = base + u * RPI + lane / LPR;
-      float x[8];
-      {
-        const uint32_t w4[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+      float x[16];
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        const uint32_t w4[4] = {raw[u][hc].x, raw[u][hc].y, raw[u][hc].z, raw[u][hc].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          x[2 * i] = __uint_as_float(w4[i] << 16);
-          x[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+          x[8 * hc + 2 * i] = __uint_as_float(w4[i] << 16);
+          x[8 * hc + 2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
         }
       }
       if (p.gamma != nullptr) {
         float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+        for (int i = 0; i < 16; ++i) ss = fmaf(x[i], x[i], ss);
 #pragma unroll
         for (int off = LPR / 2; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         const float rstd = rsqrtf(ss * (1.f / (float)D) + p.eps);   // D is a power of two: exact
         if (p.rstd != nullptr && sub == 0 && r < rows) p.rstd[rs_idx[u]] = rstd;
-        const float4 g0 = ldg4(p.gamma + e0), g1 = ldg4(p.gamma + e0 + 4);
-        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const uint32_t v = pack2(x[i] * rstd * g[i], x[i + 1] * rstd * g[i + 1]);   // bf16 rounding
-          x[i] = __uint_as_float(v << 16);
-          x[i + 1] = __uint_as_float(v & 0xffff0000u);
-        }
-      }
-      const bool rot = pos[u] >= 0 && pos[u] < p.cache_seq_len;
-      const float* cs = p.cache + (int64_t)(rot ? pos[u] : 0) * D;
-      if constexpr (NEOX) {
-        float y[8];
+        for (int hc = 0; hc < 2; ++hc) {
+          const int e = 8 * (hc ? c1 : c0);
+          const float4 g0 = ldg4(p.gamma + e), g1 = ldg4(p.gamma + e + 4);
+          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = __shfl_xor_sync(0xffffffffu, x[i], LPR / 2);
-        if (rot) {
-          // lanes with d < D/2 hold a (x' = a c - b s), the others b (x' = a s + b c):
-          // both are x' = x c + y s' with s' = -s in the first half, y the partner
-          const bool first = sub < LPR / 2;
-          const int i0 = first ? e0 : e0 - D / 2;
-          const float4 c0 = ldg4(cs + i0), c1 = ldg4(cs + i0 + 4);
-          const float4 s0 = ldg4(cs + D / 2 + i0), s1 = ldg4(cs + D / 2 + i0 + 4);
-          const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          const float sg = first ? -1.f : 1.f;
-          const float sn[8] = {s0.x * sg, s0.y * sg, s0.z * sg, s0.w * sg, s1.x * sg, s1.y * sg, s1.z * sg, s1.w * sg};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) x[i] = x[i] * c[i] + y[i] * sn[i];
-        }
-      } else {
-        if (rot) {
-          const float4 c = ldg4(cs + e0 / 2), sn = ldg4(cs + D / 2 + e0 / 2);
-          const float cc[4] = {c.x, c.y, c.z, c.w}, ss4[4] = {sn.x, sn.y, sn.z, sn.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float a = x[2 * i], bb = x[2 * i + 1];
-            x[2 * i] = a * cc[i] - bb * ss4[i];
-            x[2 * i + 1] = a * ss4[i] + bb * cc[i];
+          for (int i = 0; i < 8; i += 2) {
+            const uint32_t v = pack2(x[8 * hc + i] * rstd * g[i], x[8 * hc + i + 1] * rstd * g[i + 1]);   // bf16
+            x[8 * hc + i] = __uint_as_float(v << 16);
+            x[8 * hc + i + 1] = __uint_as_float(v & 0xffff0000u);
           }
         }
       }
-      if (r < rows)
-        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + out_off[u]) =
+      if (pos[u] >= 0 && pos[u] < p.cache_seq_len) {
+        const float* cs = p.cache + (int64_t)pos[u] * D;
+        const float4 ca = ldg4(cs + ci), cb = ldg4(cs + ci + 4);
+        const float4 sa = ldg4(cs + D / 2 + ci), sb = ldg4(cs + D / 2 + ci + 4);
+        const float c[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+        const float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          // NeoX: element i of chunk c0 pairs with element i of chunk c1;
+          // interleaved: elements 2i and 2i + 1 of the lane's 16
+          const int ia = NEOX ? i : 2 * i, ib = NEOX ? 8 + i : 2 * i + 1;
+          const float av = x[ia], bv = x[ib];
+          x[ia] = av * c[i] - bv * sn[i];
+          x[ib] = av * sn[i] + bv * c[i];
+        }
+      }
+      if (r < rows) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + out_off[u];
+        *reinterpret_cast<uint4*>(dst + 8 * c0) =
             make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+        *reinterpret_cast<uint4*>(dst + 8 * c1) =
+            make_uint4(pack2(x[8], x[9]), pack2(x[10], x[11]), pack2(x[12], x[13]), pack2(x[14], x[15]));
+      }
     }
   }
 }
@@ -178,7 +178,7 @@ cudaError_t launch_f32_to_bf16(const float* src, int64_t sb, int64_t sh, int64_t
 cudaError_t launch_norm_rope(const NormRopeParams& p, int num_sms, cudaStream_t stream) {
   const int64_t rows = (int64_t)p.B * p.H * p.S;
   if (rows == 0) return cudaSuccess;
-  const int64_t rows_per_block = 8 * (32 / (p.D / 8)) * kGroups;
+  const int64_t rows_per_block = 8 * (32 / (p.D / 16)) * kGroups;
   int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   const int64_t cap = (int64_t)num_sms * kMinBlocks;
   if (blocks > cap) blocks = cap;
