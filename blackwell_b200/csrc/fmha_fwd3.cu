@@ -333,6 +333,83 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
   float2* xch = reinterpret_cast<float2*>(smem + L::kX);
   uint32_t tc = 0, itn = 0;
 
+  // Segment epilogue: merge the row's parts ((m, l) exchanged through shared
+  // memory), read O_0 .. O_{N-1} once PV of the segment's last tile is done,
+  // write O (this thread's D / N columns) and LSE, and free O for the next
+  // segment's first PV.  It runs after the next segment's first tile, so that
+  // the wait for the last PV and the exchange overlap that tile's softmax
+  // (the next segment's first PV waits on O-free, so O is intact until then).
+  bool pend = false;
+  float pm = 0.f, pl = 0.f;
+  int prow = 0, pb = 0, ph = 0;
+  uint32_t pitn = 0;
+  auto epilogue = [&](const float m_run, const float l_run, const int row, const int b, const int h,
+                      const uint32_t itn) -> bool {
+    // merge the parts of the row: exchange (m, l) through shared memory
+    xch[part * kRows + rl] = make_float2(m_run, l_run);
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&bars.xch);
+    if (!wc.wait(&bars.xch, itn & 1)) return false;
+    float mp[N], lp[N];
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+      const float2 v = xch[q * kRows + rl];
+      mp[q] = v.x;
+      lp[q] = v.y;
+    }
+    float m = mp[0];
+#pragma unroll
+    for (int q = 1; q < N; ++q) m = fmaxf(m, mp[q]);
+    float wq[N], lsum = 0.f;
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+      wq[q] = mp[q] == -INFINITY ? 0.f : ex2_mufu(mp[q] - m);
+      lsum = fmaf(lp[q], wq[q], lsum);
+    }
+    const float inv_l = 1.f / lsum;
+#pragma unroll
+    for (int q = 0; q < N; ++q) wq[q] *= inv_l;
+    if (!wc.wait(&bars.o_full, itn & 1)) return false;
+    tc_fence_after();
+    // this thread writes output columns [part DC, part DC + DC) = sum over q of O_q * w_q
+    const uint32_t o0 = tmem + lane_off + Split<D>::kOCol + part * DC;
+    float acc[DC];
+#pragma unroll
+    for (int i = 0; i < DC; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+#pragma unroll
+      for (int c0 = 0; c0 < DC; c0 += (DC < 32 ? DC : 32)) {
+        if constexpr (DC >= 32) {
+          uint32_t x[32];
+          tmem_ld32(o0 + q * D + c0, x);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
+        } else {
+          uint32_t x[16];
+          tmem_ld16(o0 + q * D + c0, x);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
+        }
+      }
+    }
+    // O has been read: the next item's first PV may overwrite it
+    tc_fence_before();
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&bars.o_empty);
+    if (row < p.Sq) {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.O) + b * p.o_sb + h * p.o_sh +
+                                            (int64_t)row * p.o_ss + part * DC);
+#pragma unroll
+      for (int i = 0; i < DC / 8; ++i)
+        dst[i] = make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
+                            pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
+      if (p.LSE != nullptr && part == 0)
+        p.LSE[((int64_t)b * p.Hq + h) * p.lse_sh + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
+    }
+    return true;
+  };
+
   for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
     const Item3 it = decode_item3(p, idx);
     for (int sg = 0; sg < it.nseg; ++sg) {
@@ -430,73 +507,24 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
       BW_TRACE_AT(t == 0, 3, g);
       BW_TRACE_AT(t == 128, 5, g);
       BW_TRACE_AT((t & 31) == 0 && t < 256, 10 + (t >> 5), g);
-    }
-    // merge the parts of the row: exchange (m, l) through shared memory
-    xch[part * kRows + rl] = make_float2(m_run, l_run);
-    __syncwarp();
-    if ((t & 31) == 0) mbar_arrive(&bars.xch);
-    if (!wc.wait(&bars.xch, itn & 1)) return;
-    float mp[N], lp[N];
-#pragma unroll
-    for (int q = 0; q < N; ++q) {
-      const float2 v = xch[q * kRows + rl];
-      mp[q] = v.x;
-      lp[q] = v.y;
-    }
-    float m = mp[0];
-#pragma unroll
-    for (int q = 1; q < N; ++q) m = fmaxf(m, mp[q]);
-    float wq[N], lsum = 0.f;
-#pragma unroll
-    for (int q = 0; q < N; ++q) {
-      wq[q] = mp[q] == -INFINITY ? 0.f : ex2_mufu(mp[q] - m);
-      lsum = fmaf(lp[q], wq[q], lsum);
-    }
-    const float inv_l = 1.f / lsum;
-#pragma unroll
-    for (int q = 0; q < N; ++q) wq[q] *= inv_l;
-    if (!wc.wait(&bars.o_full, itn & 1)) return;
-    tc_fence_after();
-    // this thread writes output columns [part DC, part DC + DC) = sum over q of O_q * w_q
-    const uint32_t o0 = tmem + lane_off + Split<D>::kOCol + part * DC;
-    float acc[DC];
-#pragma unroll
-    for (int i = 0; i < DC; ++i) acc[i] = 0.f;
-#pragma unroll
-    for (int q = 0; q < N; ++q) {
-#pragma unroll
-      for (int c0 = 0; c0 < DC; c0 += (DC < 32 ? DC : 32)) {
-        if constexpr (DC >= 32) {
-          uint32_t x[32];
-          tmem_ld32(o0 + q * D + c0, x);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
-        } else {
-          uint32_t x[16];
-          tmem_ld16(o0 + q * D + c0, x);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
-        }
+      if (j == 0 && pend) {
+        if (!epilogue(pm, pl, prow, pb, ph, pitn)) return;
+        pend = false;
       }
     }
-    // O has been read: the next item's first PV may overwrite it
-    tc_fence_before();
-    __syncwarp();
-    if ((t & 31) == 0) mbar_arrive(&bars.o_empty);
-    if (row < p.Sq) {
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.O) + it.b * p.o_sb + it.h * p.o_sh +
-                                            (int64_t)row * p.o_ss + part * DC);
-#pragma unroll
-      for (int i = 0; i < DC / 8; ++i)
-        dst[i] = make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
-                            pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
-      if (p.LSE != nullptr && part == 0)
-        p.LSE[((int64_t)it.b * p.Hq + it.h) * p.lse_sh + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
-    }
+    // this segment's epilogue runs after the next segment's first tile
+    pend = true;
+    pm = m_run;
+    pl = l_run;
+    prow = row;
+    pb = it.b;
+    ph = it.h;
+    pitn = itn;
     tc += n;
     ++itn;
     }
   }
+  if (pend) epilogue(pm, pl, prow, pb, ph, pitn);
 }
 
 template <int D, int POLY>
