@@ -14,7 +14,8 @@
 namespace {
 
 // Device error word: 0, or 0x100|site for a timed-out wait, 0x200 for a decode
-// workspace overflow.  One per device (module globals are per context).
+// workspace overflow, 0x400 for a shared-memory window the prefill kernel
+// could not align.  One per device (module globals are per context).
 __device__ int g_bw_err;
 
 constexpr int kMaxDevices = 64;
@@ -75,6 +76,21 @@ int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, 
                         const_cast<void*>(base), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
+}
+
+// 4-D store map over the [B, Hq, Sq, D] bf16 output with element strides
+// st (sb, sh, ss, 1): box (D / 2, 32, 1, 1), the half row one thread of the
+// prefill kernel writes for the 32 rows of a warp; 128-byte swizzle for
+// D = 128 (64-column boxes), 64-byte for D = 64.
+int make_map_out(CUtensorMap* m, void* base, int B, int H, int S, int D, const int64_t st[3]) {
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
+  cuuint32_t box[4] = {(cuuint32_t)(D / 2), 32, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
 }
 
@@ -142,6 +158,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
   if (make_map_bhsd(&maps.k, K, B, Hkv, Skv, D, st.k, kv_rows) != BW_OK) return BW_ERR_CUDA;
   if (make_map_bhsd(&maps.v, V, B, Hkv, Skv, D, st.v, kv_rows) != BW_OK) return BW_ERR_CUDA;
+  if (kern == 3 && make_map_out(&maps.o, O, B, Hq, Sq, D, st.o) != BW_OK) return BW_ERR_CUDA;
 
   bw::FmhaParams p{};
   p.O = O;
@@ -578,6 +595,7 @@ int bw_stream_status(void* stream) {
     if (cudaMemcpy(dev->err, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return BW_ERR_CUDA;
   }
   if (v == 0) return BW_OK;
+  if (v & 0x400) return BW_ERR_CUDA;
   if (v & 0x200) return BW_ERR_WORKSPACE;
   return BW_ERR_TIMEOUT;
 }

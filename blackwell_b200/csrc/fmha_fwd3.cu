@@ -45,7 +45,10 @@ namespace bw {
 namespace {
 
 constexpr int kRows = 128;
-constexpr int kSmemBudget = 232448 - 2048;
+// The dynamic shared memory window is requested 512 bytes larger than the
+// layout, for the round-up of its base to 1024 bytes (the kernel checks it).
+constexpr int kAlignSlack = 512;
+constexpr int kSmemBudget = 232448 - kAlignSlack;
 constexpr int kMaxSlots = 12;
 
 // N threads per query row, each taking kKeys = 128 / N keys of every key tile
@@ -72,12 +75,18 @@ struct L3 {
   static constexpr int kQ = 0;                  // two Q slots: the next segment's tile loads during this one
   static constexpr int kKV = 2 * kTile;
   static constexpr int kXBytes = Split<D>::N * kRows * 8;     // (m, l) exchange: [N parts][128 rows] float2
-  static constexpr int kNSraw = (kSmemBudget - kKV - 512 - kXBytes) / kTile;
+  // output staging: each softmax warp's 32 rows x D / N columns, in the
+  // swizzled layout of the O tensor map (one TMA store per warp and segment)
+  static constexpr int kStgWarp = 32 * (D / Split<D>::N) * 2;
+  static constexpr int kNSraw = (kSmemBudget - kKV - kTile - 512 - kXBytes) / kTile;
   static constexpr int NS = kNSraw > kMaxSlots ? kMaxSlots : kNSraw;
-  static constexpr int kBar = kKV + NS * kTile;
+  static constexpr int kStg = kKV + NS * kTile;
+  static constexpr int kBar = kStg + kTile;
   static constexpr int kX = kBar + 512;
   static constexpr int kBytes = kX + kXBytes;
   static_assert(NS >= 4, "K/V ring needs at least 4 slots");
+  static_assert(kBytes + kAlignSlack <= 232448, "shared memory");
+  static_assert(kStgWarp * 4 * Split<D>::N == kTile, "staging = one tile");
 };
 
 struct Bars3 {
@@ -320,7 +329,8 @@ __device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
 // Thread t (0 .. 128 N - 1): row t % 128 of the item's tile (TMEM lane), part
 // t / 128, i.e. keys part K .. part K + K - 1 of every key tile (K = 128 / N).
 template <int D, int POLY>
-__device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
+__device__ void softmax3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc,
+                         uint32_t tmem, int t) {
   using L = L3<D>;
   constexpr int N = Split<D>::N;
   constexpr int K = Split<D>::kKeys;
@@ -346,6 +356,9 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
   auto epilogue = [&](const float m_run, const float l_run, const int row, const int b, const int h,
                       const uint32_t itn) -> bool {
     // merge the parts of the row: exchange (m, l) through shared memory
+    BW_TRACE_AT(t == 0, 40, itn);
+    // the warp's previous output store has read its staging area
+    if ((t & 31) == 0) bulk_wait_read0();
     xch[part * kRows + rl] = make_float2(m_run, l_run);
     __syncwarp();
     if ((t & 31) == 0) mbar_arrive(&bars.xch);
@@ -397,16 +410,30 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
     tc_fence_before();
     __syncwarp();
     if ((t & 31) == 0) mbar_arrive(&bars.o_empty);
-    if (row < p.Sq) {
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.O) + b * p.o_sb + h * p.o_sh +
-                                            (int64_t)row * p.o_ss + part * DC);
+    // O rows go out through the warp's staging area and one TMA store (each
+    // thread's row is 16-byte chunks at the swizzled positions of the map's
+    // layout, so the writes are free of bank conflicts; rows past Sq are
+    // clipped by the map)
+    {
+      const int ln = t & 31;
+      uint8_t* stg = smem + L::kStg + (t >> 5) * L::kStgWarp;
 #pragma unroll
-      for (int i = 0; i < DC / 8; ++i)
-        dst[i] = make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
-                            pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
-      if (p.LSE != nullptr && part == 0)
-        p.LSE[((int64_t)b * p.Hq + h) * p.lse_sh + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
+      for (int i = 0; i < DC / 8; ++i) {
+        const int pos = DC == 64 ? (i ^ (ln & 7)) : (i ^ ((ln >> 1) & 3));
+        *reinterpret_cast<uint4*>(stg + ln * (DC * 2) + pos * 16) =
+            make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
+                       pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (ln == 0) {
+        tma_store_4d(&maps.o, stg, part * DC, row - ln, h, b);
+        bulk_commit();
+      }
     }
+    if (p.LSE != nullptr && part == 0 && row < p.Sq)
+      p.LSE[((int64_t)b * p.Hq + h) * p.lse_sh + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
+    BW_TRACE_AT(t == 0, 44, itn);
     return true;
   };
 
@@ -531,7 +558,13 @@ template <int D, int POLY>
 __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
   using L = L3<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad > (uint32_t)kAlignSlack) {
+    // the window cannot hold the 1024-aligned layout: report, do nothing
+    if (threadIdx.x == 0) atomicCAS(p.err, 0, 0x400);
+    return;
+  }
+  uint8_t* smem = smem_raw + pad;
   Bars3& bars = *reinterpret_cast<Bars3*>(smem + L::kBar);
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -565,6 +598,7 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
     prefetch_tmap(&maps.q);
     prefetch_tmap(&maps.k);
     prefetch_tmap(&maps.v);
+    prefetch_tmap(&maps.o);
   }
   if (warp == kPvIssuer) tmem_alloc(&bars.tmem_base, 512);
   tc_fence_before();
@@ -574,7 +608,9 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
   WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, warp};
 
   if (warp < kSoftWarps) {
-    softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
+    softmax3<D, POLY>(p, maps, smem, bars, wc, tmem, tid);
+    // the warp's output stores read shared memory until they complete
+    if (lane == 0) bulk_wait0();
   } else if (warp == kProducer) {
     if (lane == 0) producer3<D>(p, maps, smem, bars, wc);
   } else {
@@ -593,7 +629,7 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
 
 template <int D, int POLY>
 cudaError_t launch3(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
-  constexpr int bytes = L3<D>::kBytes + 1024;
+  constexpr int bytes = L3<D>::kBytes + kAlignSlack;
   auto kern = fmha_fwd3_kernel<D, POLY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
