@@ -35,7 +35,7 @@ std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
 std::atomic<int64_t> g_exp_poly{2};
-std::atomic<int64_t> g_prefill_kernel{0};   // 0: by head dimension (3 for D = 128, 1 for D = 64)
+std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 3)
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -80,16 +80,15 @@ int make_map_bhsd(CUtensorMap* m, const void* base, int B, int H, int S, int D, 
 }
 
 // 4-D store map over the [B, Hq, Sq, D] bf16 output with element strides
-// st (sb, sh, ss, 1): box (D / 2, 32, 1, 1), the half row one thread of the
-// prefill kernel writes for the 32 rows of a warp; 128-byte swizzle for
-// D = 128 (64-column boxes), 64-byte for D = 64.
+// st (sb, sh, ss, 1): box (64, 32, 1, 1), one 128-byte-swizzled panel of the
+// 32 rows an epilogue warp of the prefill kernel writes (D / 64 stores).
 int make_map_out(CUtensorMap* m, void* base, int B, int H, int S, int D, const int64_t st[3]) {
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
-  cuuint32_t box[4] = {(cuuint32_t)(D / 2), 32, 1, 1};
+  cuuint32_t box[4] = {64, 32, 1, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BW_OK : BW_ERR_CUDA;
 }
@@ -150,7 +149,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
 
   if (q_offset < 0 || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
   int kern = (int)g_prefill_kernel.load();
-  if (kern == 0) kern = D == 128 ? 3 : 1;
+  if (kern == 0) kern = 3;
   if (kern == 2 && q_offset != 0) kern = 1;   // kernel 2 has no query offset
   const bool v2 = kern == 2;
   const uint32_t kv_rows = v2 ? 64u : 128u;

@@ -8,18 +8,22 @@
 // GQA_sm103_causal_v3.cu:2156-2180) and the split-length launcher
 // (src/SM120/attention/adhitya_GQA.cu:199-213).
 //
-// Design (one persistent CTA per SM, 4 N + 3 warps, N = 2):
+// Design (one persistent CTA per SM, four warpgroups, N = 2):
 //   warps 0 .. 4N-1  softmax: one 128-row query tile; row r is shared by
 //                    thread r of warps 4q .. 4q+3 for q = 0 .. N-1 ("part" q
 //                    takes keys qK .. qK+K-1 of every key tile, K = 128 / N)
-//   warp 4N          TMA producer: the Q tile, then K and V tiles in MMA order
-//   warp 4N+1        PV MMA issuer (one thread) and TMEM owner
-//   warp 4N+2        QK^T MMA issuer (one thread)
+//   warps 8 .. 11    epilogue: row r of each finished tile (merge, O, LSE)
+//   warp 12          TMA producer: the Q tile, then K and V tiles in MMA order
+//   warp 13          PV MMA issuer (one thread) and TMEM owner
+//   warp 14          QK^T MMA issuer (one thread); warp 15 idle
 // The parts of a row run independent online softmaxes (own running max and
 // sum) into their own accumulators O_q = sum over part-q keys of p V, and are
-// merged once per row at the end:
+// merged once per row by the epilogue warps:
 //   m = max_q m_q, w_q = 2^(m_q - m), L = sum_q l_q w_q,
-//   O = sum_q O_q w_q / L,  LSE = ln 2 (m + log2 L).
+//   O = sum_q O_q w_q / L,  LSE = ln 2 (m + log2 L),
+// so the softmax warps go from a tile's last key tile straight to the next
+// tile's first (the merge, the O read and its store cost ~1.5k cycles per
+// tile, which on the softmax warps stalled the whole pipeline).
 // Tensor memory: S_0 .. S_{NB-1} (128 fp32 columns each; NB = 2 at D = 128,
 // 3 at D = 64) | O_0 .. O_{N-1} (D columns each).  Global key tile g (counted
 // over all items of the CTA) uses score buffer g % NB; part q writes its P
@@ -63,7 +67,10 @@ struct Split {
   static constexpr int NB = D == 128 ? 2 : 3;
   static constexpr int kKeys = 128 / N;
   static constexpr int kOCol = NB * 128;          // first TMEM column of O_0
-  static constexpr int kThreads = 128 * N + 96;   // + producer, PV issuer, QK issuer warps
+  // softmax (4 N warps), output epilogue (4 warps), producer / PV issuer /
+  // QK issuer (+ one idle warp): four warpgroups for the register split
+  static constexpr int kThreads = 512;
+  static_assert(N == 2, "warpgroup roles assume two softmax warpgroups");
   static_assert(NB * 128 + N * D <= 512, "TMEM: score buffers and accumulators");
 };
 
@@ -74,10 +81,11 @@ struct L3 {
   static constexpr int kPanels = D / 64;
   static constexpr int kQ = 0;                  // two Q slots: the next segment's tile loads during this one
   static constexpr int kKV = 2 * kTile;
-  static constexpr int kXBytes = Split<D>::N * kRows * 8;     // (m, l) exchange: [N parts][128 rows] float2
-  // output staging: each softmax warp's 32 rows x D / N columns, in the
-  // swizzled layout of the O tensor map (one TMA store per warp and segment)
-  static constexpr int kStgWarp = 32 * (D / Split<D>::N) * 2;
+  static constexpr int kXBytes = Split<D>::N * kRows * 8;     // (m, l) per row and part: [N][128] float2
+  // output staging: each epilogue warp's 32 rows x D columns as D / 64
+  // panels of 32 x 128 bytes in the 128-byte-swizzled layout of the O tensor
+  // map (one TMA store per panel)
+  static constexpr int kStgWarp = 32 * D * 2;
   static constexpr int kNSraw = (kSmemBudget - kKV - kTile - 512 - kXBytes) / kTile;
   static constexpr int NS = kNSraw > kMaxSlots ? kMaxSlots : kNSraw;
   static constexpr int kStg = kKV + NS * kTile;
@@ -86,11 +94,12 @@ struct L3 {
   static constexpr int kBytes = kX + kXBytes;
   static_assert(NS >= 4, "K/V ring needs at least 4 slots");
   static_assert(kBytes + kAlignSlack <= 232448, "shared memory");
-  static_assert(kStgWarp * 4 * Split<D>::N == kTile, "staging = one tile");
+  static_assert(kStgWarp * 4 == kTile, "staging = one tile");
 };
 
 struct Bars3 {
-  uint64_t q_full[2], q_empty[2], s_full[3], p_full[3], pv_done[3], o_full, o_empty, mma_done, qk_done, xch;
+  uint64_t q_full[2], q_empty[2], s_full[3], p_full[3], pv_done[3], o_full, o_empty, mma_done, qk_done;
+  uint64_t xch_full, xch_empty;
   uint64_t kv_full[kMaxSlots], kv_empty[kMaxSlots];
   uint32_t tmem_base;
   int abort_flag;
@@ -329,12 +338,9 @@ __device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
 // Thread t (0 .. 128 N - 1): row t % 128 of the item's tile (TMEM lane), part
 // t / 128, i.e. keys part K .. part K + K - 1 of every key tile (K = 128 / N).
 template <int D, int POLY>
-__device__ void softmax3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc,
-                         uint32_t tmem, int t) {
+__device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
   using L = L3<D>;
-  constexpr int N = Split<D>::N;
   constexpr int K = Split<D>::kKeys;
-  constexpr int DC = D / N;                 // output columns this thread writes
   const int rl = t & 127, part = t >> 7;
   const uint32_t lane_off = (uint32_t)((rl >> 5) * 32) << 16;
   constexpr uint32_t NB = Split<D>::NB;
@@ -342,100 +348,6 @@ __device__ void softmax3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sme
   const float c = p.scale_log2;
   float2* xch = reinterpret_cast<float2*>(smem + L::kX);
   uint32_t tc = 0, itn = 0;
-
-  // Segment epilogue: merge the row's parts ((m, l) exchanged through shared
-  // memory), read O_0 .. O_{N-1} once PV of the segment's last tile is done,
-  // write O (this thread's D / N columns) and LSE, and free O for the next
-  // segment's first PV.  It runs after the next segment's first tile, so that
-  // the wait for the last PV and the exchange overlap that tile's softmax
-  // (the next segment's first PV waits on O-free, so O is intact until then).
-  bool pend = false;
-  float pm = 0.f, pl = 0.f;
-  int prow = 0, pb = 0, ph = 0;
-  uint32_t pitn = 0;
-  auto epilogue = [&](const float m_run, const float l_run, const int row, const int b, const int h,
-                      const uint32_t itn) -> bool {
-    // merge the parts of the row: exchange (m, l) through shared memory
-    BW_TRACE_AT(t == 0, 40, itn);
-    // the warp's previous output store has read its staging area
-    if ((t & 31) == 0) bulk_wait_read0();
-    xch[part * kRows + rl] = make_float2(m_run, l_run);
-    __syncwarp();
-    if ((t & 31) == 0) mbar_arrive(&bars.xch);
-    if (!wc.wait(&bars.xch, itn & 1)) return false;
-    float mp[N], lp[N];
-#pragma unroll
-    for (int q = 0; q < N; ++q) {
-      const float2 v = xch[q * kRows + rl];
-      mp[q] = v.x;
-      lp[q] = v.y;
-    }
-    float m = mp[0];
-#pragma unroll
-    for (int q = 1; q < N; ++q) m = fmaxf(m, mp[q]);
-    float wq[N], lsum = 0.f;
-#pragma unroll
-    for (int q = 0; q < N; ++q) {
-      wq[q] = mp[q] == -INFINITY ? 0.f : ex2_mufu(mp[q] - m);
-      lsum = fmaf(lp[q], wq[q], lsum);
-    }
-    const float inv_l = 1.f / lsum;
-#pragma unroll
-    for (int q = 0; q < N; ++q) wq[q] *= inv_l;
-    if (!wc.wait(&bars.o_full, itn & 1)) return false;
-    tc_fence_after();
-    // this thread writes output columns [part DC, part DC + DC) = sum over q of O_q * w_q
-    const uint32_t o0 = tmem + lane_off + Split<D>::kOCol + part * DC;
-    float acc[DC];
-#pragma unroll
-    for (int i = 0; i < DC; ++i) acc[i] = 0.f;
-#pragma unroll
-    for (int q = 0; q < N; ++q) {
-#pragma unroll
-      for (int c0 = 0; c0 < DC; c0 += (DC < 32 ? DC : 32)) {
-        if constexpr (DC >= 32) {
-          uint32_t x[32];
-          tmem_ld32(o0 + q * D + c0, x);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
-        } else {
-          uint32_t x[16];
-          tmem_ld16(o0 + q * D + c0, x);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[c0 + i] = fmaf(__uint_as_float(x[i]), wq[q], acc[c0 + i]);
-        }
-      }
-    }
-    // O has been read: the next item's first PV may overwrite it
-    tc_fence_before();
-    __syncwarp();
-    if ((t & 31) == 0) mbar_arrive(&bars.o_empty);
-    // O rows go out through the warp's staging area and one TMA store (each
-    // thread's row is 16-byte chunks at the swizzled positions of the map's
-    // layout, so the writes are free of bank conflicts; rows past Sq are
-    // clipped by the map)
-    {
-      const int ln = t & 31;
-      uint8_t* stg = smem + L::kStg + (t >> 5) * L::kStgWarp;
-#pragma unroll
-      for (int i = 0; i < DC / 8; ++i) {
-        const int pos = DC == 64 ? (i ^ (ln & 7)) : (i ^ ((ln >> 1) & 3));
-        *reinterpret_cast<uint4*>(stg + ln * (DC * 2) + pos * 16) =
-            make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
-                       pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (ln == 0) {
-        tma_store_4d(&maps.o, stg, part * DC, row - ln, h, b);
-        bulk_commit();
-      }
-    }
-    if (p.LSE != nullptr && part == 0 && row < p.Sq)
-      p.LSE[((int64_t)b * p.Hq + h) * p.lse_sh + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
-    BW_TRACE_AT(t == 0, 44, itn);
-    return true;
-  };
 
   for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
     const Item3 it = decode_item3(p, idx);
@@ -534,24 +446,107 @@ __device__ void softmax3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sme
       BW_TRACE_AT(t == 0, 3, g);
       BW_TRACE_AT(t == 128, 5, g);
       BW_TRACE_AT((t & 31) == 0 && t < 256, 10 + (t >> 5), g);
-      if (j == 0 && pend) {
-        if (!epilogue(pm, pl, prow, pb, ph, pitn)) return;
-        pend = false;
-      }
     }
-    // this segment's epilogue runs after the next segment's first tile
-    pend = true;
-    pm = m_run;
-    pl = l_run;
-    prow = row;
-    pb = it.b;
-    ph = it.h;
-    pitn = itn;
+    // hand the row's (m, l) to the epilogue warps (once they have read the
+    // previous segment's) and go on with the next segment
+    if (itn > 0 && !wc.wait(&bars.xch_empty, (itn - 1) & 1)) return;
+    xch[part * kRows + rl] = make_float2(m_run, l_run);
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&bars.xch_full);
     tc += n;
     ++itn;
     }
   }
-  if (pend) epilogue(pm, pl, prow, pb, ph, pitn);
+}
+
+// ---------------------------------------------------------- epilogue warps
+// Thread t (0 .. 127): row t of every segment's query tile (TMEM lane t).  Per
+// segment: merge the parts of the row from their (m, l) (m = max_q m_q,
+// w_q = 2^(m_q - m) / L, L = sum_q l_q 2^(m_q - m)), read O_0 .. O_{N-1} once
+// PV of the segment's last tile is done, free O for the next segment's first
+// PV, and write O = sum_q w_q O_q through the warp's staging area with TMA
+// stores (rows past Sq are clipped by the map) and LSE = ln 2 (m + log2 L).
+// The softmax warps never wait for any of this unless they finish a whole
+// segment before the previous one's (m, l) has been read.
+template <int D>
+__device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc,
+                          uint32_t tmem, int t) {
+  using L = L3<D>;
+  constexpr int N = Split<D>::N;
+  const int ln = t & 31, wq = t >> 5;
+  const uint32_t o0 = tmem + ((uint32_t)(wq * 32) << 16) + Split<D>::kOCol;
+  const float2* xch = reinterpret_cast<const float2*>(smem + L::kX);
+  uint8_t* stg = smem + L::kStg + wq * L::kStgWarp;
+  uint32_t itn = 0;
+  for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
+    const Item3 it = decode_item3(p, idx);
+    for (int sg = 0; sg < it.nseg; ++sg) {
+      const int qt = sg == 0 ? it.qt[0] : it.qt[1];
+      const int row = qt * kRows + t;
+      if (!wc.wait(&bars.xch_full, itn & 1)) return;
+      float mp[N], lp[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) {
+        const float2 v = xch[q * kRows + t];
+        mp[q] = v.x;
+        lp[q] = v.y;
+      }
+      __syncwarp();
+      if (ln == 0) mbar_arrive(&bars.xch_empty);
+      float m = mp[0];
+#pragma unroll
+      for (int q = 1; q < N; ++q) m = fmaxf(m, mp[q]);
+      float w[N], lsum = 0.f;
+#pragma unroll
+      for (int q = 0; q < N; ++q) {
+        w[q] = mp[q] == -INFINITY ? 0.f : ex2_mufu(mp[q] - m);
+        lsum = fmaf(lp[q], w[q], lsum);
+      }
+      const float inv_l = 1.f / lsum;
+#pragma unroll
+      for (int q = 0; q < N; ++q) w[q] *= inv_l;
+      if (ln == 0) bulk_wait_read0();   // the warp's previous stores have read the staging area
+      __syncwarp();
+      if (!wc.wait(&bars.o_full, itn & 1)) return;
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        float acc[32];
+        uint32_t x[32];
+        tmem_ld32(o0 + c0, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(x[i]) * w[0];
+#pragma unroll
+        for (int q = 1; q < N; ++q) {
+          tmem_ld32(o0 + q * D + c0, x);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(x[i]), w[q], acc[i]);
+        }
+        // columns c0 .. c0 + 31: panel c0 / 64, 16-byte chunks (c0 % 64) / 8 + i
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int ch = (c0 & 63) / 8 + i;
+          *reinterpret_cast<uint4*>(stg + (c0 / 64) * (32 * 128) + ln * 128 + ((ch ^ (ln & 7)) << 4)) =
+              make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
+                         pack_bf16_3(acc[8 * i + 4], acc[8 * i + 5]), pack_bf16_3(acc[8 * i + 6], acc[8 * i + 7]));
+        }
+      }
+      // O has been read: the next segment's first PV may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (ln == 0) mbar_arrive(&bars.o_empty);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (ln == 0) {
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) tma_store_4d(&maps.o, stg + c * (32 * 128), c * 64, row - ln, it.h, it.b);
+        bulk_commit();
+      }
+      if (p.LSE != nullptr && row < p.Sq)
+        p.LSE[((int64_t)it.b * p.Hq + it.h) * p.lse_sh + row] = (m + __log2f(lsum)) * 0.69314718055994531f;
+      ++itn;
+    }
+  }
 }
 
 template <int D, int POLY>
@@ -570,7 +565,8 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
   const int warp = tid >> 5;
   const int lane = tid & 31;
   constexpr int kSoftWarps = 4 * Split<D>::N;
-  constexpr int kProducer = kSoftWarps, kPvIssuer = kSoftWarps + 1;
+  constexpr int kEpilogue = kSoftWarps;                     // warpgroup 2
+  constexpr int kProducer = kSoftWarps + 4, kPvIssuer = kSoftWarps + 5, kQkIssuer = kSoftWarps + 6;
 
   if (tid == 0) {
     for (int b = 0; b < 2; ++b) {
@@ -584,8 +580,9 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
     for (int b = 0; b < Split<D>::NB; ++b) mbar_init(&bars.pv_done[b], 1);
     mbar_init(&bars.qk_done, 1);
     mbar_init(&bars.o_full, 1);
-    mbar_init(&bars.o_empty, 4 * Split<D>::N);
-    mbar_init(&bars.xch, 4 * Split<D>::N);
+    mbar_init(&bars.o_empty, 4);                     // one arrival per epilogue warp
+    mbar_init(&bars.xch_full, 4 * Split<D>::N);      // one per softmax warp
+    mbar_init(&bars.xch_empty, 4);
     mbar_init(&bars.mma_done, 1);
     for (int s = 0; s < L::NS; ++s) {
       mbar_init(&bars.kv_full[s], 1);
@@ -607,16 +604,23 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
   const uint32_t tmem = bars.tmem_base;
   WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, warp};
 
+  // Register split (the block is launched with 128 per thread, 65536 in all):
+  // softmax 2 x 128 x 168 + epilogue 128 x 128 + producer / issuers 128 x 40
+  // = 64512.
   if (warp < kSoftWarps) {
-    softmax3<D, POLY>(p, maps, smem, bars, wc, tmem, tid);
+    reg_alloc<168>();
+    softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
+  } else if (warp < kEpilogue + 4) {
+    reg_dealloc<128>();   // keeps the launch count; states this role's bound to the register allocator
+    epilogue3<D>(p, maps, smem, bars, wc, tmem, tid - 32 * kEpilogue);
     // the warp's output stores read shared memory until they complete
     if (lane == 0) bulk_wait0();
-  } else if (warp == kProducer) {
-    if (lane == 0) producer3<D>(p, maps, smem, bars, wc);
   } else {
+    reg_dealloc<40>();
     if (lane == 0) {
-      if (warp == kPvIssuer) pv_issuer3<D>(p, smem, bars, wc, tmem);
-      else qk_issuer3<D>(p, smem, bars, wc, tmem);
+      if (warp == kProducer) producer3<D>(p, maps, smem, bars, wc);
+      else if (warp == kPvIssuer) pv_issuer3<D>(p, smem, bars, wc, tmem);
+      else if (warp == kQkIssuer) qk_issuer3<D>(p, smem, bars, wc, tmem);
     }
   }
   tc_fence_before();

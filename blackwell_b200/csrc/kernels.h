@@ -32,8 +32,8 @@ struct FmhaParams {
 struct FmhaMaps {
   CUtensorMap q, k, v;           // 4-D (D, S, H, B) bf16, box (64, rows, 1, 1), SWIZZLE_128B;
                                  // rows = 128 for Q; 128 (launch_fmha_fwd) or 64 (launch_fmha_fwd2) for K, V
-  CUtensorMap o;                 // launch_fmha_fwd3 only: 4-D (D, Sq, Hq, B) bf16 output, box (D / 2, 32, 1, 1),
-                                 // SWIZZLE_128B (D = 128) or SWIZZLE_64B (D = 64)
+  CUtensorMap o;                 // launch_fmha_fwd3 only: 4-D (D, Sq, Hq, B) bf16 output, box (64, 32, 1, 1),
+                                 // SWIZZLE_128B
 };
 
 // exp_poly: of every 8 pairs of exponentials, how many run as the FMA-pipe
