@@ -35,7 +35,7 @@ std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
 std::atomic<int64_t> g_exp_poly{2};
-std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 3)
+std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 4, or 3 for causal D = 64)
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -149,7 +149,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
 
   if (q_offset < 0 || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
   int kern = (int)g_prefill_kernel.load();
-  if (kern == 0) kern = 3;
+  if (kern == 0) kern = (D == 128 || !causal) ? 4 : 3;
   if (kern == 2 && q_offset != 0) kern = 1;   // kernel 2 has no query offset
   const bool v2 = kern == 2;
   const uint32_t kv_rows = v2 ? 64u : 128u;
@@ -157,7 +157,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
   if (make_map_bhsd(&maps.k, K, B, Hkv, Skv, D, st.k, kv_rows) != BW_OK) return BW_ERR_CUDA;
   if (make_map_bhsd(&maps.v, V, B, Hkv, Skv, D, st.v, kv_rows) != BW_OK) return BW_ERR_CUDA;
-  if (kern == 3 && make_map_out(&maps.o, O, B, Hq, Sq, D, st.o) != BW_OK) return BW_ERR_CUDA;
+  if (kern >= 3 && make_map_out(&maps.o, O, B, Hq, Sq, D, st.o) != BW_OK) return BW_ERR_CUDA;
 
   bw::FmhaParams p{};
   p.O = O;
@@ -178,7 +178,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   p.n_kvtiles = (Skv + 127) / 128;
   p.pair_heads = (G % 2 == 0) ? 1 : 0;
   p.num_items = p.pair_heads ? B * (Hq / 2) * p.n_qtiles : B * Hq * ((p.n_qtiles + 1) / 2);
-  if (kern == 3) p.num_items = B * Hq * (causal ? (p.n_qtiles + 1) / 2 : p.n_qtiles);
+  if (kern >= 3) p.num_items = B * Hq * (causal ? (p.n_qtiles + 1) / 2 : p.n_qtiles);
   p.err = dev->err;
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.debug_flags = (int)g_debug_flags.load();
@@ -188,7 +188,8 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   const int64_t cap = g_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = (int)cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = kern == 3 ? bw::launch_fmha_fwd3(p, maps, (int)g_exp_poly.load(), ctas, s)
+  cudaError_t e = kern == 4 ? bw::launch_fmha_fwd4(p, maps, (int)g_exp_poly.load(), ctas, s)
+                  : kern == 3 ? bw::launch_fmha_fwd3(p, maps, (int)g_exp_poly.load(), ctas, s)
                   : v2      ? bw::launch_fmha_fwd2(p, maps, (int)g_exp_poly.load(), ctas, s)
                             : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas, s);
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
@@ -612,7 +613,7 @@ int bw_set_option(int key, int64_t value) {
       g_max_ctas = value;
       return BW_OK;
     case BW_OPT_PREFILL_KERNEL:
-      if (value < 0 || value > 3) return BW_ERR_SHAPE;
+      if (value < 0 || value > 4) return BW_ERR_SHAPE;
       g_prefill_kernel = value;
       return BW_OK;
     case BW_OPT_EXP_POLY:

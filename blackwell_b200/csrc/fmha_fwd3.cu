@@ -61,17 +61,26 @@ constexpr int kMaxSlots = 12;
 // D = 128: N = 2, NB = 2.  D = 64: N = 2, NB = 3 (the third buffer lets
 // QK(g + 1) start before PV(g - 1) has finished; N = 4 with two buffers
 // measured slower, the PV -> QK chain bounding it).
-template <int D>
+//
+// Variant V = 4 (kernel 4) keeps one accumulator O and three score buffers
+// (TMEM S_0 | S_1 | S_2 | O, 3 x 128 + D <= 512 columns), so that QK(g + 1)
+// never waits for PV(g - 1): each softmax warp covers 16 rows of its TMEM
+// lane quadrant through the 16-lane access shapes, four threads per row and
+// two rows per thread, and the four threads of a row share one running max
+// (two shuffles per row and tile), so all keys of a row accumulate into the
+// same O.
+template <int D, int V>
 struct Split {
-  static constexpr int N = 2;
-  static constexpr int NB = D == 128 ? 2 : 3;
-  static constexpr int kKeys = 128 / N;
-  static constexpr int kOCol = NB * 128;          // first TMEM column of O_0
+  static constexpr int N = 2;                      // softmax warpgroups
+  static constexpr int NACC = V == 3 ? 2 : 1;      // O accumulators
+  static constexpr int NB = (V == 4 || D == 64) ? 3 : 2;
+  static constexpr int kKeys = 128 / N;            // keys per part (V = 3)
+  static constexpr int kOCol = NB * 128;           // first TMEM column of O_0
   // softmax (4 N warps), output epilogue (4 warps), producer / PV issuer /
   // QK issuer (+ one idle warp): four warpgroups for the register split
   static constexpr int kThreads = 512;
   static_assert(N == 2, "warpgroup roles assume two softmax warpgroups");
-  static_assert(NB * 128 + N * D <= 512, "TMEM: score buffers and accumulators");
+  static_assert(NB * 128 + NACC * D <= 512, "TMEM: score buffers and accumulators");
 };
 
 template <int D>
@@ -81,7 +90,7 @@ struct L3 {
   static constexpr int kPanels = D / 64;
   static constexpr int kQ = 0;                  // two Q slots: the next segment's tile loads during this one
   static constexpr int kKV = 2 * kTile;
-  static constexpr int kXBytes = Split<D>::N * kRows * 8;     // (m, l) per row and part: [N][128] float2
+  static constexpr int kXBytes = 2 * kRows * 8;   // (m, l) per row and accumulator: [2][128] float2
   // output staging: each epilogue warp's 32 rows x D columns as D / 64
   // panels of 32 x 128 bytes in the 128-byte-swizzled layout of the O tensor
   // map (one TMA store per panel)
@@ -231,7 +240,7 @@ __device__ __forceinline__ uint32_t pos_v(int j, int n) {
   return j <= n - 2 ? (uint32_t)(2 + 2 * j) : (uint32_t)(2 * n - 1);
 }
 
-template <int D>
+template <int D, int V>
 __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
   using L = L3<D>;
   constexpr int NS = L::NS;
@@ -252,7 +261,7 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
       ++qn;
       const uint32_t qa = q_lo + qs * (uint32_t)(L::kTile / 16);
       for (int j = 0; j < n; ++j) {
-        constexpr uint32_t NB = Split<D>::NB;
+        constexpr uint32_t NB = Split<D, V>::NB;
         const uint32_t g = tc + j, buf = g % NB;
         const uint32_t e = e0 + pos_k(j);
         if (!wc.wait(&bars.kv_full[e % NS], (e / NS) & 1)) { ok = false; break; }
@@ -280,7 +289,7 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
   drain_wait(&bars.qk_done, 0, wc.timeout_ns);
 }
 
-template <int D>
+template <int D, int V>
 __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
   using L = L3<D>;
   constexpr int NS = L::NS;
@@ -295,7 +304,7 @@ __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
     for (int sg = 0; ok && sg < it.nseg; ++sg) {
       const int n = sg == 0 ? it.n[0] : it.n[1];
       for (int j = 0; j < n; ++j) {
-        constexpr uint32_t NB = Split<D>::NB;
+        constexpr uint32_t NB = Split<D, V>::NB;
         const uint32_t g = tc + j, buf = g % NB;
         const uint32_t e = e0 + pos_v(j, n);
         if (!wc.wait(&bars.kv_full[e % NS], (e / NS) & 1)) { ok = false; break; }
@@ -305,14 +314,22 @@ __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
         BW_TRACE_AT(true, 6, g);
         tc_fence_after();
         const uint32_t va = v_lo0 + (e % NS) * (uint32_t)(L::kTile / 16);
-        // part q: O_q += P_q (TMEM columns q K .. q K + K/2 - 1 of the buffer, K = keys
-        // per part) * V rows q K .. q K + K - 1; k-step ks covers V rows 16 ks .. 16 ks + 15
-        constexpr int KSP = Split<D>::kKeys / 16;   // k-steps per part
+        if constexpr (V == 3) {
+          // part q: O_q += P_q (TMEM columns q K .. q K + K/2 - 1 of the buffer, K = keys
+          // per part) * V rows q K .. q K + K - 1; k-step ks covers V rows 16 ks .. 16 ks + 15
+          constexpr int KSP = Split<D, V>::kKeys / 16;   // k-steps per part
 #pragma unroll
-        for (int ks = 0; ks < kRows / 16; ++ks) {
-          const int q = ks / KSP, kin = ks % KSP;
-          mma_ts_lh(tmem + Split<D>::kOCol + q * D, tmem + buf * 128 + q * Split<D>::kKeys + kin * 8, va + (ks * 16 * 128) / 16,
-                    HI, IDESC_PV, (kin > 0 || j > 0) ? 1u : 0u);
+          for (int ks = 0; ks < kRows / 16; ++ks) {
+            const int q = ks / KSP, kin = ks % KSP;
+            mma_ts_lh(tmem + Split<D, V>::kOCol + q * D, tmem + buf * 128 + q * Split<D, V>::kKeys + kin * 8,
+                      va + (ks * 16 * 128) / 16, HI, IDESC_PV, (kin > 0 || j > 0) ? 1u : 0u);
+          }
+        } else {
+          // O += P (bf16, key k at column k / 2 of the buffer) * V; k-step ks: keys 16 ks ..
+#pragma unroll
+          for (int ks = 0; ks < kRows / 16; ++ks)
+            mma_ts_lh(tmem + Split<D, V>::kOCol, tmem + buf * 128 + ks * 8, va + (ks * 16 * 128) / 16, HI, IDESC_PV,
+                      (ks > 0 || j > 0) ? 1u : 0u);
         }
         BW_TRACE_AT(true, 8, g);
         tc_commit(&bars.pv_done[buf]);
@@ -340,11 +357,12 @@ __device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
 template <int D, int POLY>
 __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
   using L = L3<D>;
-  constexpr int K = Split<D>::kKeys;
+  using Split = bw::Split<D, 3>;
+  constexpr int K = Split::kKeys;
   const int rl = t & 127, part = t >> 7;
   const uint32_t lane_off = (uint32_t)((rl >> 5) * 32) << 16;
-  constexpr uint32_t NB = Split<D>::NB;
-  const uint32_t o_own = tmem + lane_off + Split<D>::kOCol + part * D;
+  constexpr uint32_t NB = Split::NB;
+  const uint32_t o_own = tmem + lane_off + Split::kOCol + part * D;
   const float c = p.scale_log2;
   float2* xch = reinterpret_cast<float2*>(smem + L::kX);
   uint32_t tc = 0, itn = 0;
@@ -459,6 +477,174 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
   }
 }
 
+// ------------------------------------------------- softmax warps, kernel 4
+// Warp w (0 .. 7) covers TMEM lanes 32 (w % 4) + 16 (w / 4) .. + 15 with the
+// 16-lane shapes: thread i holds rows r0 = that base + i / 4 and r1 = r0 + 8,
+// keys 8 c + 2 (i % 4) and + 1 of chunk c = 0 .. 15 of every key tile (64
+// scores, 32 per row).  The four threads of a row (lanes 4k .. 4k + 3) reduce
+// the tile max with two shuffles and so keep the same running max; each keeps
+// its own partial row sum, reduced at the end of the query tile.  P (bf16)
+// goes back over the first 64 columns of the score buffer in the order the PV
+// MMA reads it (key k at column k / 2).
+template <int D, int POLY>
+__device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
+  using L = L3<D>;
+  using Split = bw::Split<D, 4>;
+  constexpr uint32_t NB = Split::NB;
+  const int w = t >> 5, ln = t & 31;
+  const int rb = 32 * (w & 3) + 16 * (w >> 2);           // first TMEM lane of the warp
+  const int r0 = rb + (ln >> 2), kq = 2 * (ln & 3);      // rows r0, r0 + 8; key offset in a chunk
+  const uint32_t lane_off = (uint32_t)rb << 16;
+  const uint32_t o_tm = tmem + lane_off + Split::kOCol;
+  const float c = p.scale_log2;
+  float2* xch = reinterpret_cast<float2*>(smem + L::kX);
+  uint32_t tc = 0, itn = 0;
+
+  for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
+    const Item3 it = decode_item3(p, idx);
+    for (int sg = 0; sg < it.nseg; ++sg) {
+    const int n = sg == 0 ? it.n[0] : it.n[1];
+    const int qt = sg == 0 ? it.qt[0] : it.qt[1];
+    const int row0 = qt * kRows + r0;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const uint32_t g = tc + j, buf = g % NB;
+      const uint32_t s_tmem = tmem + lane_off + buf * 128;
+      if (!wc.wait(&bars.s_full[buf], (g / NB) & 1)) return;
+      BW_TRACE_AT(t == 0, 0, g);
+      tc_fence_after();
+      uint32_t r[64];
+      tmem_ld_16x256b_x16(s_tmem, r);
+      BW_TRACE_AT(t == 0, 1, g);
+      float* s = reinterpret_cast<float*>(r);
+      const int kv0 = j * kRows;
+      if ((p.causal && kv0 + kRows - 1 > p.q_offset + qt * kRows) || kv0 + kRows > p.Skv) {
+        int lim0 = p.Skv - kv0, lim1 = lim0;
+        if (p.causal) {
+          lim0 = min(lim0, p.q_offset + row0 + 1 - kv0);
+          lim1 = min(lim1, p.q_offset + row0 + 9 - kv0);
+        }
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          const int k = 8 * ch + kq;
+          if (k >= lim0) s[4 * ch] = -INFINITY;
+          if (k + 1 >= lim0) s[4 * ch + 1] = -INFINITY;
+          if (k >= lim1) s[4 * ch + 2] = -INFINITY;
+          if (k + 1 >= lim1) s[4 * ch + 3] = -INFINITY;
+        }
+      }
+      float mx0, mx1;
+      {
+        float a0 = fmaxf(s[0], s[1]), b0 = fmaxf(s[4], s[5]), a1 = fmaxf(s[2], s[3]), b1 = fmaxf(s[6], s[7]);
+#pragma unroll
+        for (int ch = 2; ch < 16; ch += 2) {
+          a0 = fmax3(a0, s[4 * ch], s[4 * ch + 1]);
+          b0 = fmax3(b0, s[4 * ch + 4], s[4 * ch + 5]);
+          a1 = fmax3(a1, s[4 * ch + 2], s[4 * ch + 3]);
+          b1 = fmax3(b1, s[4 * ch + 6], s[4 * ch + 7]);
+        }
+        mx0 = fmaxf(a0, b0);
+        mx1 = fmaxf(a1, b1);
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      }
+      // lazy rescale per row (the same decision in the row's four threads)
+      const float mc0 = mx0 * c, mc1 = mx1 * c;
+      float corr0 = 1.f, corr1 = 1.f;
+      const bool up0 = mc0 > m0 + 8.f, up1 = mc1 > m1 + 8.f;
+      if (up0) {
+        corr0 = ex2_mufu(m0 - mc0);
+        m0 = mc0;
+      }
+      if (up1) {
+        corr1 = ex2_mufu(m1 - mc1);
+        m1 = mc1;
+      }
+      const float ms0 = (m0 == -INFINITY) ? 0.f : m0, ms1 = (m1 == -INFINITY) ? 0.f : m1;
+      const f2 cc2{c, c}, nm0{-ms0, -ms0}, nm1{-ms1, -ms1};
+      f2 sa0{0.f, 0.f}, sb0{0.f, 0.f}, sa1{0.f, 0.f}, sb1{0.f, 0.f};
+      // pair k: chunk k / 2, row k & 1 (registers 4 (k / 2) + 2 (k & 1) and + 1)
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const int i = 4 * (k >> 1) + 2 * (k & 1);
+        const f2 x = ffma2(f2{s[i], s[i + 1]}, cc2, (k & 1) ? nm1 : nm0);
+        f2 e;
+        if ((k & 7) < POLY) {
+          e = ex2_poly2(x);
+        } else {
+          e.x = ex2_mufu(x.x);
+          e.y = ex2_mufu(x.y);
+        }
+        s[i] = e.x;
+        s[i + 1] = e.y;
+        if ((k & 1) == 0) {
+          if ((k & 2) == 0) sa0 = fadd2(sa0, e);
+          else sb0 = fadd2(sb0, e);
+        } else {
+          if ((k & 2) == 0) sa1 = fadd2(sa1, e);
+          else sb1 = fadd2(sb1, e);
+        }
+      }
+      sa0 = fadd2(sa0, sb0);
+      sa1 = fadd2(sa1, sb1);
+      l0 = l0 * corr0 + (sa0.x + sa0.y);
+      l1 = l1 * corr1 + (sa1.x + sa1.y);
+      BW_TRACE_AT(t == 0, 2, g);
+      {
+        // 16x128b repetition ch: column 4 ch + i % 4 (keys 8 ch + 2 (i % 4), + 1) of rows r0, r0 + 8
+        uint32_t pk[32];
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          pk[2 * ch] = pack_bf16_3(s[4 * ch], s[4 * ch + 1]);
+          pk[2 * ch + 1] = pack_bf16_3(s[4 * ch + 2], s[4 * ch + 3]);
+        }
+        tmem_st_16x128b_x16(s_tmem, pk);
+      }
+      if (j > 0 && __any_sync(0xffffffffu, up0 || up1)) {
+        // O must hold PV(j - 1) before it is rescaled
+        if (!wc.wait(&bars.pv_done[(g - 1) % NB], ((g - 1) / NB) & 1)) return;
+        tc_fence_after();
+        if constexpr (D == 128) {
+          uint32_t o[64];
+          tmem_ld_16x256b_x16(o_tm, o);
+#pragma unroll
+          for (int i = 0; i < 64; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * ((i & 2) ? corr1 : corr0));
+          tmem_st_16x256b_x16(o_tm, o);
+        } else {
+          uint32_t o[32];
+          tmem_ld_16x256b_x8(o_tm, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * ((i & 2) ? corr1 : corr0));
+          tmem_st_16x256b_x8(o_tm, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (ln == 0) mbar_arrive(&bars.p_full[buf]);
+      BW_TRACE_AT(t == 0, 3, g);
+      BW_TRACE_AT(ln == 0 && t < 256, 10 + w, g);
+    }
+    // the row sums of the four threads, then (m, l) per row for the epilogue
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if (itn > 0 && !wc.wait(&bars.xch_empty, (itn - 1) & 1)) return;
+    if ((ln & 3) == 0) {
+      xch[r0] = make_float2(m0, l0);
+      xch[r0 + 8] = make_float2(m1, l1);
+    }
+    __syncwarp();
+    if (ln == 0) mbar_arrive(&bars.xch_full);
+    tc += n;
+    ++itn;
+    }
+  }
+}
+
 // ---------------------------------------------------------- epilogue warps
 // Thread t (0 .. 127): row t of every segment's query tile (TMEM lane t).  Per
 // segment: merge the parts of the row from their (m, l) (m = max_q m_q,
@@ -468,13 +654,14 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
 // stores (rows past Sq are clipped by the map) and LSE = ln 2 (m + log2 L).
 // The softmax warps never wait for any of this unless they finish a whole
 // segment before the previous one's (m, l) has been read.
-template <int D>
+// (Kernel 4: one accumulator, N = 1 below: O / L.)
+template <int D, int V>
 __device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc,
                           uint32_t tmem, int t) {
   using L = L3<D>;
-  constexpr int N = Split<D>::N;
+  constexpr int N = Split<D, V>::NACC;
   const int ln = t & 31, wq = t >> 5;
-  const uint32_t o0 = tmem + ((uint32_t)(wq * 32) << 16) + Split<D>::kOCol;
+  const uint32_t o0 = tmem + ((uint32_t)(wq * 32) << 16) + Split<D, V>::kOCol;
   const float2* xch = reinterpret_cast<const float2*>(smem + L::kX);
   uint8_t* stg = smem + L::kStg + wq * L::kStgWarp;
   uint32_t itn = 0;
@@ -549,8 +736,10 @@ __device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sm
   }
 }
 
-template <int D, int POLY>
-__global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
+template <int D, int POLY, int V>
+__global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
+  using Split = bw::Split<D, V>;
+  static_assert(Split::kThreads == 512, "launch bounds");
   using L = L3<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -564,7 +753,7 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  constexpr int kSoftWarps = 4 * Split<D>::N;
+  constexpr int kSoftWarps = 4 * Split::N;
   constexpr int kEpilogue = kSoftWarps;                     // warpgroup 2
   constexpr int kProducer = kSoftWarps + 4, kPvIssuer = kSoftWarps + 5, kQkIssuer = kSoftWarps + 6;
 
@@ -573,15 +762,15 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
       mbar_init(&bars.q_full[b], 1);
       mbar_init(&bars.q_empty[b], 1);
     }
-    for (int b = 0; b < Split<D>::NB; ++b) {
+    for (int b = 0; b < Split::NB; ++b) {
       mbar_init(&bars.s_full[b], 1);
-      mbar_init(&bars.p_full[b], 4 * Split<D>::N);   // one arrival per softmax warp
+      mbar_init(&bars.p_full[b], 4 * Split::N);   // one arrival per softmax warp
     }
-    for (int b = 0; b < Split<D>::NB; ++b) mbar_init(&bars.pv_done[b], 1);
+    for (int b = 0; b < Split::NB; ++b) mbar_init(&bars.pv_done[b], 1);
     mbar_init(&bars.qk_done, 1);
     mbar_init(&bars.o_full, 1);
     mbar_init(&bars.o_empty, 4);                     // one arrival per epilogue warp
-    mbar_init(&bars.xch_full, 4 * Split<D>::N);      // one per softmax warp
+    mbar_init(&bars.xch_full, 4 * Split::N);         // one per softmax warp
     mbar_init(&bars.xch_empty, 4);
     mbar_init(&bars.mma_done, 1);
     for (int s = 0; s < L::NS; ++s) {
@@ -609,18 +798,19 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
   // = 64512.
   if (warp < kSoftWarps) {
     reg_alloc<168>();
-    softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
+    if constexpr (V == 3) softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
+    else softmax4<D, POLY>(p, smem, bars, wc, tmem, tid);
   } else if (warp < kEpilogue + 4) {
     reg_dealloc<128>();   // keeps the launch count; states this role's bound to the register allocator
-    epilogue3<D>(p, maps, smem, bars, wc, tmem, tid - 32 * kEpilogue);
+    epilogue3<D, V>(p, maps, smem, bars, wc, tmem, tid - 32 * kEpilogue);
     // the warp's output stores read shared memory until they complete
     if (lane == 0) bulk_wait0();
   } else {
     reg_dealloc<40>();
     if (lane == 0) {
       if (warp == kProducer) producer3<D>(p, maps, smem, bars, wc);
-      else if (warp == kPvIssuer) pv_issuer3<D>(p, smem, bars, wc, tmem);
-      else if (warp == kQkIssuer) qk_issuer3<D>(p, smem, bars, wc, tmem);
+      else if (warp == kPvIssuer) pv_issuer3<D, V>(p, smem, bars, wc, tmem);
+      else if (warp == kQkIssuer) qk_issuer3<D, V>(p, smem, bars, wc, tmem);
     }
   }
   tc_fence_before();
@@ -631,24 +821,24 @@ __global__ void __launch_bounds__(Split<D>::kThreads, 1) fmha_fwd3_kernel(const 
   }
 }
 
-template <int D, int POLY>
+template <int D, int POLY, int V>
 cudaError_t launch3(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
   constexpr int bytes = L3<D>::kBytes + kAlignSlack;
-  auto kern = fmha_fwd3_kernel<D, POLY>;
+  auto kern = fmha_fwd3_kernel<D, POLY, V>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
   const int grid = p.num_items < num_sms ? p.num_items : num_sms;
-  kern<<<grid, Split<D>::kThreads, bytes, stream>>>(p, maps);
+  kern<<<grid, Split<D, V>::kThreads, bytes, stream>>>(p, maps);
   return cudaGetLastError();
 }
 
-template <int D>
+template <int D, int V>
 cudaError_t launch3_poly(const FmhaParams& p, const FmhaMaps& maps, int poly, int num_sms, cudaStream_t stream) {
   switch (poly) {
-    case 0: return launch3<D, 0>(p, maps, num_sms, stream);
-    case 2: return launch3<D, 2>(p, maps, num_sms, stream);
-    case 3: return launch3<D, 3>(p, maps, num_sms, stream);
-    case 4: return launch3<D, 4>(p, maps, num_sms, stream);
+    case 0: return launch3<D, 0, V>(p, maps, num_sms, stream);
+    case 2: return launch3<D, 2, V>(p, maps, num_sms, stream);
+    case 3: return launch3<D, 3, V>(p, maps, num_sms, stream);
+    case 4: return launch3<D, 4, V>(p, maps, num_sms, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -657,8 +847,15 @@ cudaError_t launch3_poly(const FmhaParams& p, const FmhaMaps& maps, int poly, in
 
 cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream) {
-  if (p.D == 128) return launch3_poly<128>(p, maps, exp_poly, num_sms, stream);
-  if (p.D == 64) return launch3_poly<64>(p, maps, exp_poly, num_sms, stream);
+  if (p.D == 128) return launch3_poly<128, 3>(p, maps, exp_poly, num_sms, stream);
+  if (p.D == 64) return launch3_poly<64, 3>(p, maps, exp_poly, num_sms, stream);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_fmha_fwd4(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
+                             cudaStream_t stream) {
+  if (p.D == 128) return launch3_poly<128, 4>(p, maps, exp_poly, num_sms, stream);
+  if (p.D == 64) return launch3_poly<64, 4>(p, maps, exp_poly, num_sms, stream);
   return cudaErrorInvalidValue;
 }
 

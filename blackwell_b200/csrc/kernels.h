@@ -57,6 +57,11 @@ cudaError_t launch_fmha_fwd2(const FmhaParams& p, const FmhaMaps& maps, int exp_
 // One query tile per work item, double-buffered scores (one softmax warpgroup).
 cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream);
+// Kernel 4: kernel 3's roles with one O accumulator and three score buffers
+// (rows read through the 16-lane TMEM shapes, four threads per row sharing
+// the running max).
+cudaError_t launch_fmha_fwd4(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
+                             cudaStream_t stream);
 
 // Split-KV single-token decode over ragged, contiguous per-sequence KV.
 struct DecodeParams {

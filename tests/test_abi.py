@@ -138,9 +138,9 @@ def test_new_entry_points_validate_without_gpu():
 def test_prefill_kernel_option_values():
     lib = _ffi.lib()
     old = lib.bw_get_option(_ffi.BW_OPT_PREFILL_KERNEL)
-    assert old == 0                                   # default: chosen by head dimension
-    for v in (0, 1, 2, 3):
+    assert old == 0                                   # default kernel
+    for v in (0, 1, 2, 3, 4):
         assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == 0
-    for v in (-1, 4):
+    for v in (-1, 5):
         assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == _ffi.BW_ERR_SHAPE
     lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, old)

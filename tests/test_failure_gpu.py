@@ -12,11 +12,11 @@ from tests._util import seeded_bf16
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kernel,D", [(0, 64), (0, 128), (1, 128), (3, 64)],
-                         ids=["auto_d64", "auto_d128", "k1_d128", "k3_d64"])
+@pytest.mark.parametrize("kernel,D", [(0, 64), (0, 128), (1, 128), (1, 64), (4, 128), (4, 64)],
+                         ids=["auto_d64", "auto_d128", "k1_d128", "k1_d64", "k4_d128", "k4_d64"])
 def test_withheld_tile_reports_timeout_and_recovers(kernel, D):
-    """Each prefill kernel (kernel 3 is the D = 128 default, kernel 1 the D = 64
-    one): the withheld K tile makes every role's bounded wait expire."""
+    """Each prefill kernel at both head dimensions: the withheld K tile makes
+    every role's bounded wait expire."""
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
     q = seeded_bf16((1, 2, 256, D), 1).cuda()
