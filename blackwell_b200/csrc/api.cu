@@ -35,7 +35,7 @@ std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
 std::atomic<int64_t> g_exp_poly{2};
-std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 4, or 3 for causal D = 64)
+std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 4)
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -149,7 +149,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
 
   if (q_offset < 0 || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
   int kern = (int)g_prefill_kernel.load();
-  if (kern == 0) kern = (D == 128 || !causal) ? 4 : 3;
+  if (kern == 0) kern = 4;
   if (kern == 2 && q_offset != 0) kern = 1;   // kernel 2 has no query offset
   const bool v2 = kern == 2;
   const uint32_t kv_rows = v2 ? 64u : 128u;

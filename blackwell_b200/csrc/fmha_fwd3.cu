@@ -1,5 +1,7 @@
-// GQA / MHA flash-attention forward for sm_100a, one query tile per work item
-// with double-buffered scores.
+// GQA / MHA flash-attention forward for sm_100a, one query tile per work item:
+// kernel 3 (double-buffered scores, each row split over two threads with
+// separate accumulators) and kernel 4 (three score buffers, one accumulator;
+// see Split below), the same roles and pipeline otherwise.
 //
 // Same operator as fmha_fwd.cu (per query row i of head hq, KV head hq / G:
 // O[i] = softmax(scale * Q[i] K^T) V, LSE[i] = ln sum_j exp(scale * Q[i].K[j]),

@@ -232,8 +232,8 @@ BW_API int bw_stream_status(void* stream);
  *   BW_OPT_EXP_POLY        of every 8 pairs of softmax exponentials, how many
  *                          are computed by an FMA-pipe polynomial instead of
  *                          MUFU ex2: 0, 2 (default), 3 or 4
- *   BW_OPT_PREFILL_KERNEL  0 (default): kernel 4, or kernel 3 for causal
- *                          D = 64 (the faster one for each, measured on B200);
+ *   BW_OPT_PREFILL_KERNEL  0 (default): kernel 4 (the fastest at every
+ *                          measured shape on B200);
  *                          1: two 128-row query blocks per CTA sharing each K/V
  *                          tile, one score buffer per block;
  *                          2: as 1 with 64-key tiles and two score buffers per
