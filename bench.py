@@ -330,7 +330,8 @@ def bench_prefill(shape, causal, layout, flush, steps, warmup):
 
 def bench_fused(shape, flush, steps, warmup):
     """The reference's fused op (QK-norm + RoPE + causal GQA) at a prefill shape:
-    K's prologue as its own pass, Q's inside the attention kernel."""
+    the Q and K prologues as streaming passes into a workspace, then the
+    attention kernel (bw_gqa_fused_fwd)."""
     import blackwell_b200 as bw
     B, Hq, Hkv, S, D = shape
     g = torch.Generator(device="cuda").manual_seed(42)

@@ -40,6 +40,8 @@ SIGNATURES = {
     "bw_gqa_decode_static_scratch_bytes": (_sz, []),
     "bw_gqa_decode_static": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _f, _i, _vp]),
     "bw_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "bw_decode_packed_split_floats": (_sz, [_i, _i, _i]),
+    "bw_lse_combine_packed": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     "bw_qk_norm_rope": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _f, _i, _vp, _vp]),
     "bw_gqa_fused_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "bw_gqa_causal_offset_fwd": (_i, [_vp] * 5 + [_i] * 7 + [_f, _i, _vp, _vp]),

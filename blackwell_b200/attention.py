@@ -169,8 +169,28 @@ def lse_combine(o_part, lse_part, out=None, lse=None):
     return o, lse
 
 
+def packed_split_floats(B, Hq, D):
+    """fp32 elements of one packed decode partial: O [B, Hq, D], then LSE [B, Hq],
+    padded to a multiple of 4 (the layout bw_lse_combine_packed reads)."""
+    return int(_ffi.lib().bw_decode_packed_split_floats(B, Hq, D))
+
+
+def lse_combine_packed(parts, B, Hq, D, out=None, lse=None):
+    """Merge packed partials: parts fp32 [S, packed_split_floats(B, Hq, D)]."""
+    P = packed_split_floats(B, Hq, D)
+    if parts.dim() != 2 or parts.shape[1] != P or parts.dtype != torch.float32 or not parts.is_contiguous():
+        raise ValueError(f"parts must be a contiguous fp32 [splits, {P}] tensor")
+    o = out if out is not None else torch.empty((B, Hq, D), dtype=torch.bfloat16, device=parts.device)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=parts.device)
+    rc = _ffi.lib().bw_lse_combine_packed(_ptr(parts), parts.shape[0], B, Hq, D, _ptr(o), _ptr(lse), _stream())
+    _ffi.check(rc, "bw_lse_combine_packed")
+    return o, lse
+
+
 def stream_status() -> int:
-    """Synchronise the current stream and return (and clear) the device error code."""
+    """Synchronise the current stream and return (and clear) its error code (each
+    stream has its own error word on the device)."""
     return int(_ffi.lib().bw_stream_status(_stream()))
 
 
@@ -199,17 +219,18 @@ def gqa_decode_partial(q, k, v, kv_lens, kv_offsets, scale=None, chunk=0, worksp
         raise TypeError("kv_lens must be int32 and kv_offsets int64")
     B, Hq, D = q.shape
     total, Hkv, _ = k.shape
+    o = out if out is not None else torch.empty((B, Hq, D), dtype=torch.float32, device=q.device)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
     if total == 0:  # no local keys at all: the neutral partial of the LSE merge
-        return (torch.zeros((B, Hq, D), dtype=torch.float32, device=q.device),
-                torch.full((B, Hq), float("-inf"), dtype=torch.float32, device=q.device))
+        o.zero_()
+        lse.fill_(float("-inf"))
+        return o, lse
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if workspace is None:
         workspace = torch.empty(decode_workspace_size(B, Hq, Hkv, D, total, chunk), dtype=torch.uint8,
                                 device=q.device)
-    o = out if out is not None else torch.empty((B, Hq, D), dtype=torch.float32, device=q.device)
-    if lse is None:
-        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
     rc = _ffi.lib().bw_gqa_decode_partial(_ptr(q), _ptr(k), _ptr(v), _ptr(kv_lens), _ptr(kv_offsets), _ptr(o),
                                           _ptr(lse), B, Hq, Hkv, D, int(total), float(scale), int(chunk),
                                           _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())

@@ -5,6 +5,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include <cudaTypedefs.h>
 
@@ -13,17 +14,23 @@
 
 namespace {
 
-// Device error word: 0, or 0x100|site for a timed-out wait, 0x200 for a decode
-// workspace overflow, 0x400 for a shared-memory window the prefill kernel
-// could not align.  One per device (module globals are per context).
-__device__ int g_bw_err;
+// Device error words: 0, or 0x100|site for a timed-out wait, 0x200 for a
+// decode workspace overflow, 0x400 for a shared-memory window the prefill
+// kernel could not align.  One word per stream (slot), so that calls on
+// different streams neither see nor clear each other's errors; module
+// globals are per context, so every device has its own array.  Slot 0 is
+// shared by the streams beyond the first kErrSlots - 1 distinct ones.
+constexpr int kErrSlots = 1024;
+__device__ int g_bw_err[kErrSlots];
 
 constexpr int kMaxDevices = 64;
 
 struct DeviceState {
   bool init = false;
   int num_sms = 0;
-  int* err = nullptr;
+  int* err_base = nullptr;
+  std::unordered_map<cudaStream_t, int> slot_of;
+  int next_slot = 1;
 };
 
 std::mutex g_mu;
@@ -34,8 +41,19 @@ std::atomic<int64_t> g_timeout_ns{2000000000LL};
 std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
-std::atomic<int64_t> g_exp_poly{2};
+std::atomic<int64_t> g_exp_poly{-1};        // -1: per head dimension (kExpPolyD64 / kExpPolyD128)
 std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 4)
+
+// Measured defaults of the exponential split (of every 8 pairs, how many run as
+// the FMA-pipe polynomial) per head dimension.
+constexpr int kExpPolyD128 = 2;
+constexpr int kExpPolyD64 = 2;
+
+int exp_poly_for(int D) {
+  const int64_t v = g_exp_poly.load();
+  if (v >= 0) return (int)v;
+  return D == 64 ? kExpPolyD64 : kExpPolyD128;
+}
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -46,7 +64,7 @@ int get_device_state(DeviceState** out) {
     if (cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return BW_ERR_CUDA;
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_bw_err) != cudaSuccess) return BW_ERR_CUDA;
-    st.err = static_cast<int*>(p);
+    st.err_base = static_cast<int*>(p);
     if (!g_encode) {
       cudaDriverEntryPointQueryResult q;
       void* fn = nullptr;
@@ -59,6 +77,21 @@ int get_device_state(DeviceState** out) {
   }
   *out = &st;
   return BW_OK;
+}
+
+// The error word of `stream` on this device (assigned on first use).
+int* err_slot(DeviceState* dev, void* stream) {
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = dev->slot_of.find(s);
+  int slot = 0;
+  if (it != dev->slot_of.end()) {
+    slot = it->second;
+  } else if (dev->next_slot < kErrSlots) {
+    slot = dev->next_slot++;
+    dev->slot_of.emplace(s, slot);
+  }
+  return dev->err_base + slot;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -150,9 +183,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   if (q_offset < 0 || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
   int kern = (int)g_prefill_kernel.load();
   if (kern == 0) kern = 4;
-  if (kern == 2 && q_offset != 0) kern = 1;   // kernel 2 has no query offset
-  const bool v2 = kern == 2;
-  const uint32_t kv_rows = v2 ? 64u : 128u;
+  const uint32_t kv_rows = 128u;
   bw::FmhaMaps maps;
   if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
   if (make_map_bhsd(&maps.k, K, B, Hkv, Skv, D, st.k, kv_rows) != BW_OK) return BW_ERR_CUDA;
@@ -179,7 +210,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   p.pair_heads = (G % 2 == 0) ? 1 : 0;
   p.num_items = p.pair_heads ? B * (Hq / 2) * p.n_qtiles : B * Hq * ((p.n_qtiles + 1) / 2);
   if (kern >= 3) p.num_items = B * Hq * (causal ? (p.n_qtiles + 1) / 2 : p.n_qtiles);
-  p.err = dev->err;
+  p.err = err_slot(dev, stream);
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.debug_flags = (int)g_debug_flags.load();
   p.q_offset = q_offset;
@@ -188,10 +219,10 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   const int64_t cap = g_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = (int)cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = kern == 4 ? bw::launch_fmha_fwd4(p, maps, (int)g_exp_poly.load(), ctas, s)
-                  : kern == 3 ? bw::launch_fmha_fwd3(p, maps, (int)g_exp_poly.load(), ctas, s)
-                  : v2      ? bw::launch_fmha_fwd2(p, maps, (int)g_exp_poly.load(), ctas, s)
-                            : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, (int)g_exp_poly.load(), ctas, s);
+  const int poly = exp_poly_for(D);
+  cudaError_t e = kern == 4 ? bw::launch_fmha_fwd4(p, maps, poly, ctas, s)
+                  : kern == 3 ? bw::launch_fmha_fwd3(p, maps, poly, ctas, s)
+                            : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, poly, ctas, s);
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
@@ -211,15 +242,6 @@ int attn_forward(const void* Q, const void* K, const void* V, void* O, float* LS
                  int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream,
                  int q_offset, int lse_sh) {
   return attn_fwd(Q, K, V, O, LSE, B, Hq, Hkv, Sq, Skv, G, D, scale, causal, strides, stream, q_offset, lse_sh);
-}
-int device_context(int** err, int* num_sms, void** encode_fn) {
-  DeviceState* dev = nullptr;
-  const int rc = get_device_state(&dev);
-  if (rc != BW_OK) return rc;
-  *err = dev->err;
-  *num_sms = dev->num_sms;
-  *encode_fn = reinterpret_cast<void*>(g_encode);
-  return BW_OK;
 }
 }  // namespace bw
 
@@ -311,7 +333,7 @@ int bw_mha_fwd_f32(const float* Q, const float* K, const float* V, float* O, flo
   p.n_kvtiles = (S + 127) / 128;
   p.pair_heads = 0;
   p.num_items = B * H * ((p.n_qtiles + 1) / 2);
-  p.err = dev->err;
+  p.err = err_slot(dev, stream);
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.debug_flags = 0;
   p.q_offset = 0;
@@ -328,9 +350,13 @@ size_t bw_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int64_t total
   return align256((size_t)(B + 1) * 4) + align256((size_t)parts * G * 4) + (size_t)parts * G * D * 4;
 }
 
-static int decode_impl(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets,
-                  void* O, int o_fp32, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
-                  void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace bw {
+
+int decode_run(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets, void* O,
+               int o_fp32, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
+               void* workspace, size_t workspace_bytes, void* stream) {
   if (!Q || !K || !V || !kv_lens || !kv_offsets || !O || !workspace) return BW_ERR_NULL;
   if (B <= 0 || B > 4096 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0) return BW_ERR_SHAPE;
   const int G = Hq / Hkv;
@@ -376,7 +402,7 @@ static int decode_impl(const void* Q, const void* K, const void* V, const int* k
   p.lse_part = lse_part;
   p.chunk_prefix = prefix;
   p.max_parts = (int)parts;
-  p.err = dev->err;
+  p.err = err_slot(dev, stream);
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = bw::launch_decode(p, maps, dev->num_sms, s);
@@ -401,10 +427,14 @@ static int decode_impl(const void* Q, const void* K, const void* V, const int* k
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
+}  // namespace bw
+
+extern "C" {
+
 int bw_gqa_decode(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets,
                   void* O, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
                   void* workspace, size_t workspace_bytes, void* stream) {
-  return decode_impl(Q, K, V, kv_lens, kv_offsets, O, 0, LSE, B, Hq, Hkv, D, total_tokens, scale, chunk, workspace,
+  return bw::decode_run(Q, K, V, kv_lens, kv_offsets, O, 0, LSE, B, Hq, Hkv, D, total_tokens, scale, chunk, workspace,
                      workspace_bytes, stream);
 }
 
@@ -413,7 +443,7 @@ int bw_gqa_decode_partial(const void* Q, const void* K, const void* V, const int
                           int64_t total_tokens, float scale, int chunk, void* workspace, size_t workspace_bytes,
                           void* stream) {
   if (!LSE) return BW_ERR_NULL;
-  return decode_impl(Q, K, V, kv_lens, kv_offsets, O, 1, LSE, B, Hq, Hkv, D, total_tokens, scale, chunk, workspace,
+  return bw::decode_run(Q, K, V, kv_lens, kv_offsets, O, 1, LSE, B, Hq, Hkv, D, total_tokens, scale, chunk, workspace,
                      workspace_bytes, stream);
 }
 
@@ -472,7 +502,7 @@ int bw_gqa_decode_paged(const void* Q, const void* K_cache, const void* V_cache,
   p.lse_part = lse_part;
   p.chunk_prefix = prefix;
   p.max_parts = (int)parts;
-  p.err = dev->err;
+  p.err = err_slot(dev, stream);
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.block_table = block_table;
   p.page_size = page_size;
@@ -559,16 +589,22 @@ int bw_gqa_fused_fwd(const void* Q, const void* K, const void* V, void* O, float
   return attn_fwd(q2, k2, V, O, LSE, B, Hq, Hkv, S, S, G, D, scale, causal, nullptr, stream);
 }
 
-int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
-                   float* LSE, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int combine_uniform(const float* O_part, const float* LSE_part, int64_t o_ss, int64_t l_ss, int splits, int B, int Hq,
+                    int D, void* O, float* LSE, void* stream) {
   if (!O_part || !LSE_part || !O) return BW_ERR_NULL;
   if (splits <= 0 || B <= 0 || Hq <= 0 || D <= 0 || D % 4 != 0 || D > 128) return BW_ERR_SHAPE;
-  if (!aligned16(O_part) || (reinterpret_cast<uintptr_t>(O) & 7u)) return BW_ERR_ALIGN;
+  if (!aligned16(O_part) || (reinterpret_cast<uintptr_t>(O) & 7u) || (o_ss % 4) != 0) return BW_ERR_ALIGN;
   bw::CombineParams c{};
   c.o_part = O_part;
   c.lse_part = LSE_part;
   c.chunk_prefix = nullptr;
   c.splits = splits;
+  c.o_split_stride = o_ss;
+  c.lse_split_stride = l_ss;
   c.B = B;
   c.Hq = Hq;
   c.Hkv = Hq;
@@ -583,16 +619,38 @@ int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
+}  // namespace
+
+extern "C" {
+
+int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
+                   float* LSE, void* stream) {
+  return combine_uniform(O_part, LSE_part, (int64_t)B * Hq * D, (int64_t)B * Hq, splits, B, Hq, D, O, LSE, stream);
+}
+
+size_t bw_decode_packed_split_floats(int B, int Hq, int D) {
+  if (B <= 0 || Hq <= 0 || D <= 0) return 0;
+  return (size_t)B * Hq * D + (((size_t)B * Hq + 3) & ~size_t(3));
+}
+
+int bw_lse_combine_packed(const float* parts, int splits, int B, int Hq, int D, void* O, float* LSE, void* stream) {
+  if (!parts) return BW_ERR_NULL;
+  const int64_t ss = (int64_t)bw_decode_packed_split_floats(B, Hq, D);
+  if (ss == 0) return BW_ERR_SHAPE;
+  return combine_uniform(parts, parts + (int64_t)B * Hq * D, ss, ss, splits, B, Hq, D, O, LSE, stream);
+}
+
 int bw_stream_status(void* stream) {
   DeviceState* dev = nullptr;
   int rc = get_device_state(&dev);
   if (rc != BW_OK) return rc;
   if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return BW_ERR_CUDA;
+  int* slot = err_slot(dev, stream);
   int v = 0;
-  if (cudaMemcpy(&v, dev->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return BW_ERR_CUDA;
+  if (cudaMemcpy(&v, slot, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return BW_ERR_CUDA;
   if (v != 0) {
     const int zero = 0;
-    if (cudaMemcpy(dev->err, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return BW_ERR_CUDA;
+    if (cudaMemcpy(slot, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return BW_ERR_CUDA;
   }
   if (v == 0) return BW_OK;
   if (v & 0x400) return BW_ERR_CUDA;
@@ -613,11 +671,11 @@ int bw_set_option(int key, int64_t value) {
       g_max_ctas = value;
       return BW_OK;
     case BW_OPT_PREFILL_KERNEL:
-      if (value < 0 || value > 4) return BW_ERR_SHAPE;
+      if (value < 0 || value == 2 || value > 4) return BW_ERR_SHAPE;
       g_prefill_kernel = value;
       return BW_OK;
     case BW_OPT_EXP_POLY:
-      if (value != 0 && value != 2 && value != 3 && value != 4) return BW_ERR_SHAPE;
+      if (value != -1 && value != 0 && value != 2 && value != 3 && value != 4) return BW_ERR_SHAPE;
       g_exp_poly = value;
       return BW_OK;
     default: return BW_ERR_SHAPE;

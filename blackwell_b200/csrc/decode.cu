@@ -45,7 +45,9 @@ struct DecBars {
   uint64_t full[kStages], empty[kStages];
   int abort_flag;
   int total_parts;
+  long long warp_sum[kThreads / 32];
 };
+static_assert(sizeof(DecBars) <= 128, "DecBars must fit the 128 bytes reserved at kBar");
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -122,23 +124,51 @@ __global__ void __launch_bounds__(kThreads)
     }
     bars.abort_flag = 0;
     fence_mbar_init();
-    int acc_c = 0;
-    for (int b = 0; b < p.B; ++b) {
-      prefix[b] = acc_c;
+  }
+  // Chunk prefix over the B sequences: a block-wide exclusive scan (each thread
+  // sums a contiguous run of sequences, a warp scan plus the warp totals give
+  // its offset), O(B / threads) per thread.  The counts are summed in 64 bits;
+  // when the parts exceed the workspace capacity the prefix is all zeros (no
+  // items, the combine writes empty rows) and block 0 flags BW_ERR_WORKSPACE,
+  // so no kernel reads or writes past the workspace.
+  {
+    const int per = (p.B + kThreads - 1) / kThreads;
+    const int b0 = min(tid * per, p.B), b1 = min(b0 + per, p.B);
+    long long mine = 0;
+    for (int b = b0; b < b1; ++b) {
       const int len = p.kv_lens[b];
-      acc_c += len > 0 ? (len + p.chunk - 1) / p.chunk : 0;
+      mine += len > 0 ? (len + p.chunk - 1) / p.chunk : 0;
     }
-    prefix[p.B] = acc_c;
-    bars.total_parts = acc_c * p.Hkv;
-    if (blockIdx.x == 0) {
-      for (int b = 0; b <= p.B; ++b) p.chunk_prefix[b] = prefix[b];
-      if (acc_c * p.Hkv > p.max_parts) atomicCAS(p.err, 0, 0x200);
+    long long x = mine;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    if (lane == 31) bars.warp_sum[warp] = x;
+    __syncthreads();
+    long long before = x - mine, total_c = 0;
+    for (int w = 0; w < kThreads / 32; ++w) {
+      if (w < warp) before += bars.warp_sum[w];
+      total_c += bars.warp_sum[w];
+    }
+    const bool over = total_c * p.Hkv > (long long)p.max_parts;
+    for (int b = b0; b < b1; ++b) {
+      prefix[b] = over ? 0 : (int)before;
+      const int len = p.kv_lens[b];
+      before += len > 0 ? (len + p.chunk - 1) / p.chunk : 0;
+    }
+    if (tid == 0) {
+      prefix[p.B] = over ? 0 : (int)total_c;
+      bars.total_parts = over ? 0 : (int)(total_c * p.Hkv);
+      if (over && blockIdx.x == 0) atomicCAS(p.err, 0, 0x200);
     }
   }
   for (int i = tid; i < 16 * D; i += kThreads) acc[i] = 0.f;
   __syncthreads();
+  if (blockIdx.x == 0)
+    for (int b = tid; b <= p.B; b += kThreads) p.chunk_prefix[b] = prefix[b];
   const int total = bars.total_parts;
-  if (total > p.max_parts) return;
   WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, 16 + warp};
   const uint32_t sbase = smem_u32(smem);
 
@@ -401,11 +431,11 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(const CombineParams p)
   }
   auto lse_at = [&](int i) -> float {
     if (p.chunk_prefix) return p.lse_part[((base_part + i) * p.Hkv + kvh) * p.G + gi];
-    return p.lse_part[((int64_t)i * p.B + b) * p.Hq + hq];
+    return p.lse_part[(int64_t)i * p.lse_split_stride + (int64_t)b * p.Hq + hq];
   };
   auto o_at = [&](int i) -> const float* {
     if (p.chunk_prefix) return p.o_part + (((base_part + i) * p.Hkv + kvh) * p.G + gi) * p.D;
-    return p.o_part + (((int64_t)i * p.B + b) * p.Hq + hq) * p.D;
+    return p.o_part + (int64_t)i * p.o_split_stride + ((int64_t)b * p.Hq + hq) * p.D;
   };
   float mx = -INFINITY;
   for (int i = lane; i < nsp; i += 32) mx = fmaxf(mx, lse_at(i));

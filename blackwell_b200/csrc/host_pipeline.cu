@@ -144,6 +144,15 @@ int bw_attn_fwd_host(const void* Q, const void* K, const void* V, void* O, float
   if (cudaStreamWaitEvent(ps->s_in, ps->ev_start, 0) != cudaSuccess) return BW_ERR_CUDA;
   if (cudaStreamWaitEvent(ps->s_out, ps->ev_start, 0) != cudaSuccess) return BW_ERR_CUDA;
 
+  // An error after the first enqueue still orders the caller's stream after
+  // every copy already queued on the copy-in and copy-out streams, so that a
+  // caller who frees the buffers after the error (having synchronised its
+  // stream) cannot race them.
+  auto fail = [&](int code) -> int {
+    if (cudaEventRecord(ps->ev_start, ps->s_in) == cudaSuccess) cudaStreamWaitEvent(s_cmp, ps->ev_start, 0);
+    if (cudaEventRecord(ps->ev_done, ps->s_out) == cudaSuccess) cudaStreamWaitEvent(s_cmp, ps->ev_done, 0);
+    return code;
+  };
   for (int c = 0; c < nc; ++c) {
     const int lo = bound(c), hi = bound(c + 1);
     if (hi <= lo) continue;
@@ -164,9 +173,9 @@ int bw_attn_fwd_host(const void* Q, const void* K, const void* V, void* O, float
         e = cudaMemcpyAsync(static_cast<char*>(dv) + lo * ks, static_cast<const char*>(V) + lo * ks, (hi - lo) * ks,
                             cudaMemcpyHostToDevice, ps->s_in);
     }
-    if (e != cudaSuccess || cudaEventRecord(ps->ev_in[c], ps->s_in) != cudaSuccess) return BW_ERR_CUDA;
+    if (e != cudaSuccess || cudaEventRecord(ps->ev_in[c], ps->s_in) != cudaSuccess) return fail(BW_ERR_CUDA);
     // ---- compute on the caller's stream
-    if (cudaStreamWaitEvent(s_cmp, ps->ev_in[c], 0) != cudaSuccess) return BW_ERR_CUDA;
+    if (cudaStreamWaitEvent(s_cmp, ps->ev_in[c], 0) != cudaSuccess) return fail(BW_ERR_CUDA);
     if (by_rows) {
       const size_t qoff = (size_t)lo * st.q[2], ooff = (size_t)lo * st.o[2];
       rc = bw::attn_forward(static_cast<const uint16_t*>(dq) + qoff, dk, dv, static_cast<uint16_t*>(dout) + ooff,
@@ -179,10 +188,10 @@ int bw_attn_fwd_host(const void* Q, const void* K, const void* V, void* O, float
                             LSE ? dl + (size_t)lo * Hq * S : nullptr, hi - lo, Hq, Hkv, S, S, G, D, scale, causal, &st,
                             stream, 0, S);
     }
-    if (rc != BW_OK) return rc;
-    if (cudaEventRecord(ps->ev_cmp[c], s_cmp) != cudaSuccess) return BW_ERR_CUDA;
+    if (rc != BW_OK) return fail(rc);
+    if (cudaEventRecord(ps->ev_cmp[c], s_cmp) != cudaSuccess) return fail(BW_ERR_CUDA);
     // ---- copy out
-    if (cudaStreamWaitEvent(ps->s_out, ps->ev_cmp[c], 0) != cudaSuccess) return BW_ERR_CUDA;
+    if (cudaStreamWaitEvent(ps->s_out, ps->ev_cmp[c], 0) != cudaSuccess) return fail(BW_ERR_CUDA);
     if (by_rows) {
       e = copy_rows(O, dout, layout, B, Hq, S, D, 2, lo, hi, cudaMemcpyDeviceToHost, ps->s_out);
       if (e == cudaSuccess && LSE)
@@ -196,7 +205,7 @@ int bw_attn_fwd_host(const void* Q, const void* K, const void* V, void* O, float
         e = cudaMemcpyAsync(LSE + (size_t)lo * Hq * S, dl + (size_t)lo * Hq * S, (size_t)(hi - lo) * Hq * S * 4,
                             cudaMemcpyDeviceToHost, ps->s_out);
     }
-    if (e != cudaSuccess) return BW_ERR_CUDA;
+    if (e != cudaSuccess) return fail(BW_ERR_CUDA);
   }
   // the caller's stream is ordered after the last copy-out (and the copy-in
   // stream is drained by it too, since every compute waited on a copy-in)

@@ -31,7 +31,7 @@ struct FmhaParams {
 
 struct FmhaMaps {
   CUtensorMap q, k, v;           // 4-D (D, S, H, B) bf16, box (64, rows, 1, 1), SWIZZLE_128B;
-                                 // rows = 128 for Q; 128 (launch_fmha_fwd) or 64 (launch_fmha_fwd2) for K, V
+                                 // rows = 128
   CUtensorMap o;                 // launch_fmha_fwd3 only: 4-D (D, Sq, Hq, B) bf16 output, box (64, 32, 1, 1),
                                  // SWIZZLE_128B
 };
@@ -49,10 +49,6 @@ cudaError_t launch_fmha_fwd_f32(const FmhaParams& p, const FmhaMaps& maps, int n
 // fp32 -> bf16 copy of a [B, H, S, D] tensor (contiguous destination).
 cudaError_t launch_f32_to_bf16(const float* src, int64_t sb, int64_t sh, int64_t ss, void* dst, int B, int H, int S,
                                int D, int num_sms, cudaStream_t stream);
-
-// Double-buffered-S variant: 64-row K/V tiles (maps.k / maps.v with 64-row boxes).
-cudaError_t launch_fmha_fwd2(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
-                             cudaStream_t stream);
 
 // One query tile per work item, double-buffered scores (one softmax warpgroup).
 cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
@@ -100,6 +96,8 @@ struct CombineParams {
   const float* lse_part;         // ragged: [parts, G];                     uniform: [splits, B, Hq]
   const int* chunk_prefix;       // null => uniform `splits`
   int splits;
+  int64_t o_split_stride;        // uniform: elements between splits of o_part (B * Hq * D when contiguous)
+  int64_t lse_split_stride;      // uniform: elements between splits of lse_part (B * Hq when contiguous)
   int B, Hq, Hkv, G, D;
   void* O;                       // bf16 [B, Hq, D] (strides o_sb, o_sh)
   int64_t o_sb, o_sh;
@@ -131,8 +129,12 @@ int attn_forward(const void* Q, const void* K, const void* V, void* O, float* LS
                  int Skv, int G, int D, float scale, int causal, const bw_strides* strides, void* stream,
                  int q_offset, int lse_sh);
 
-// Per-device state owned by api.cu: the device error word, the SM count and the
-// driver's cuTensorMapEncodeTiled.  Returns a bw_attn status code.
-int device_context(int** err, int* num_sms, void** encode_fn);
+// The split-KV decode + combine of bw_gqa_decode / bw_gqa_decode_partial on a
+// given scratch buffer (`workspace`, `workspace_bytes`): argument checks, tensor
+// maps, scratch layout and both launches.  o_fp32 = 1 writes fp32 O (partial
+// results).  Returns a status code.
+int decode_run(const void* Q, const void* K, const void* V, const int* kv_lens, const int64_t* kv_offsets, void* O,
+               int o_fp32, float* LSE, int B, int Hq, int Hkv, int D, int64_t total_tokens, float scale, int chunk,
+               void* workspace, size_t workspace_bytes, void* stream);
 
 }  // namespace bw

@@ -60,11 +60,27 @@ def decode_sequence_parallel(q, k_local, v_local, local_lens, local_offsets, sca
 
     q: [B, Hq, D] (same on every rank); k_local / v_local: this rank's keys,
     [local_tokens, Hkv, D], sequence b at rows [local_offsets[b], + local_lens[b]).
-    Returns (O, LSE) of the full sequences on every rank.  `local_decode` and
-    `combine` default to the native kernels; tests substitute CPU checkers."""
-    local_decode = local_decode or (lambda *a, **kw: attention.gqa_decode_partial(*a, **kw))
-    combine = combine or attention.lse_combine
-    o_part, lse_part = local_decode(q, k_local, v_local, local_lens, local_offsets, scale=scale, chunk=chunk)
-    o_all = _all_gather(o_part, group)
-    lse_all = _all_gather(lse_part, group)
-    return combine(o_all, lse_all)
+    Returns (O, LSE) of the full sequences on every rank.
+
+    One collective per step: the rank's partial O (fp32 [B, Hq, D]) and LSE
+    (fp32 [B, Hq]) are written into ONE packed buffer (O, then LSE, padded to 16
+    bytes: ``attention.packed_split_floats``) and a single all-gather brings
+    every rank's buffer; ``bw_lse_combine_packed`` merges straight from the
+    gathered [world, packed] tensor.  `local_decode` and `combine` default to the
+    native kernels; tests substitute CPU checkers (``combine`` then receives
+    strided [world, B, Hq, D] / [world, B, Hq] views of the gathered buffer)."""
+    B, Hq, D = q.shape
+    n_o = B * Hq * D
+    buf = torch.empty(attention.packed_split_floats(B, Hq, D), dtype=torch.float32, device=q.device)
+    o_view, lse_view = buf[:n_o].view(B, Hq, D), buf[n_o:n_o + B * Hq].view(B, Hq)
+    if local_decode is None:
+        attention.gqa_decode_partial(q, k_local, v_local, local_lens, local_offsets, scale=scale, chunk=chunk,
+                                     out=o_view, lse=lse_view)
+    else:
+        o_part, lse_part = local_decode(q, k_local, v_local, local_lens, local_offsets, scale=scale, chunk=chunk)
+        o_view.copy_(o_part)
+        lse_view.copy_(lse_part)
+    gathered = _all_gather(buf, group)
+    if combine is None:
+        return attention.lse_combine_packed(gathered, B, Hq, D)
+    return combine(gathered[:, :n_o].view(-1, B, Hq, D), gathered[:, n_o:n_o + B * Hq].view(-1, B, Hq))

@@ -20,7 +20,8 @@
  *  - Return codes (never exit()): BW_OK, or an error below.  Argument errors are
  *    detected before any launch.  Device-side failures (a bounded wait that
  *    timed out, a workspace that was too small for the actual lengths) are
- *    recorded in a per-device error word that bw_stream_status() reads.
+ *    recorded in the error word of the call's stream, which bw_stream_status()
+ *    reads and clears.
  */
 #ifndef BW_ATTN_H_
 #define BW_ATTN_H_
@@ -172,6 +173,17 @@ BW_API int bw_gqa_decode_static(const void* Q, const void* K, const void* V, con
 BW_API int bw_lse_combine(const float* O_part, const float* LSE_part, int splits, int B, int Hq, int D, void* O,
                    float* LSE, void* stream);
 
+/* Packed partials for a cross-GPU merge in ONE collective (new; no reference
+ * counterpart).  A packed split is fp32 [bw_decode_packed_split_floats(B, Hq, D)]:
+ * O [B, Hq, D] (as bw_gqa_decode_partial writes it), then LSE [B, Hq], then
+ * padding to a multiple of 4 floats, so that each rank's O and LSE travel in a
+ * single all-gather.  bw_lse_combine_packed merges `splits` such buffers laid
+ * end to end (the all-gather's output, 16-byte aligned) into O bf16 [B, Hq, D]
+ * and LSE fp32 [B, Hq] (may be NULL), like bw_lse_combine. */
+BW_API size_t bw_decode_packed_split_floats(int B, int Hq, int D);
+BW_API int bw_lse_combine_packed(const float* parts, int splits, int B, int Hq, int D, void* O, float* LSE,
+                                 void* stream);
+
 /* QK-norm + RoPE prologue of the reference's fused op
  * (src/SM103/attention/GQA_fused_sm103.cu:59-104; its ground truth :328-420),
  * on a [B, H, S, D] bf16 tensor X -> Y (Y may equal X).  Per row:
@@ -217,7 +229,10 @@ BW_API int bw_attn_fwd_host(const void* Q, const void* K, const void* V, void* O
                             int S, int D, float scale, int causal, int layout, int chunks, void* workspace,
                             size_t workspace_bytes, void* stream);
 
-/* Synchronise `stream`, then read and clear this device's error word.
+/* Synchronise `stream`, then read and clear the error word of `stream` on the
+ * current device.  Every stream has its own word (the first 1023 distinct
+ * streams of a device; later ones share one), so a call on one stream neither
+ * sees nor clears the errors of calls on another.
  * Returns BW_OK, BW_ERR_TIMEOUT, BW_ERR_WORKSPACE or BW_ERR_CUDA. */
 BW_API int bw_stream_status(void* stream);
 
@@ -231,14 +246,13 @@ BW_API int bw_stream_status(void* stream);
  *   BW_OPT_MAX_CTAS        cap on the persistent prefill grid (0 = SM count)
  *   BW_OPT_EXP_POLY        of every 8 pairs of softmax exponentials, how many
  *                          are computed by an FMA-pipe polynomial instead of
- *                          MUFU ex2: 0, 2 (default), 3 or 4
+ *                          MUFU ex2: 0, 2, 3 or 4; -1 (default) picks the
+ *                          measured best per head dimension
  *   BW_OPT_PREFILL_KERNEL  0 (default): kernel 4 (the fastest at every
  *                          measured shape on B200);
  *                          1: two 128-row query blocks per CTA sharing each K/V
- *                          tile, one score buffer per block;
- *                          2: as 1 with 64-key tiles and two score buffers per
- *                          block (slower: an N=64 QK^T MMA costs 3/4 of an
- *                          N=128 one);
+ *                          tile, one score buffer per block (also the fp32
+ *                          MHA kernel);
  *                          3: one query block per CTA, two score buffers, each
  *                          row's keys split over two threads with independent
  *                          softmax states merged by separate epilogue warps,

@@ -92,21 +92,27 @@ def fp64_rows(q, k, v, scale, causal, rows, q_offset=0):
     to those rows (used at the full config sizes, where the all-rows oracle would
     take hours).  ``q_offset`` (causal only) places query row i at sequence
     position q_offset + i, so it sees keys j <= q_offset + i (the chunked-prefill
-    extension; 0 is the reference's top-left alignment).  Returns O [R, D]
-    float64 and LSE [R] float64."""
-    q, k, v = _as64(q), _as64(k), _as64(v)
+    extension; 0 is the reference's top-left alignment).  Only the query rows
+    asked for and the key / value heads they read are widened to float64 (one
+    (b, kv head) at a time), so inputs of several GB stay in their own dtype.
+    Returns O [R, D] float64 and LSE [R] float64."""
+    rows = np.asarray(rows)
     Hq, Hkv = q.shape[1], k.shape[1]
     G = Hq // Hkv
-    outs, lses = [], []
-    for b, hq, i in np.asarray(rows):
-        hkv = hq // G
-        kk, vv = k[b, hkv], v[b, hkv]
-        if causal:
-            kk, vv = kk[: q_offset + i + 1], vv[: q_offset + i + 1]
-        o, l = _row_attention(q[b, hq, i : i + 1], kk, vv, scale)
-        outs.append(o[0])
-        lses.append(l[0])
-    return np.stack(outs), np.asarray(lses)
+    outs = np.empty((len(rows), q.shape[-1]))
+    lses = np.empty(len(rows))
+    kv_of = rows[:, 0] * Hkv + rows[:, 1] // G
+    for key in np.unique(kv_of):
+        b, hkv = divmod(int(key), Hkv)
+        sel = np.nonzero(kv_of == key)[0]
+        kk, vv = _as64(k[b, hkv]), _as64(v[b, hkv])
+        for r in sel:
+            hq, i = int(rows[r, 1]), int(rows[r, 2])
+            lim = q_offset + i + 1 if causal else kk.shape[0]
+            o, l = _row_attention(_as64(q[b, hq, i : i + 1]), kk[:lim], vv[:lim], scale)
+            outs[r] = o[0]
+            lses[r] = l[0]
+    return outs, lses
 
 
 def fp64_attention(q, k, v, scale):
@@ -120,9 +126,11 @@ def decode_reference(q, k, v, kv_lens, kv_offsets, scale):
 
     q: [B, Hq, D]; k/v: [total_tokens, Hkv, D]; sequence b owns tokens
     [kv_offsets[b], kv_offsets[b] + kv_lens[b]).  Each sequence is the split-length
-    reference (base/baseline_gqa_split.py:33-48) with Sq = 1, Skv = L_b.
+    reference (base/baseline_gqa_split.py:33-48) with Sq = 1, Skv = L_b; the G
+    query heads that share a KV head are evaluated together (independent rows of
+    the same matrix product).  Only one sequence's keys are widened to float64 at
+    a time, so k / v may be large tensors in their own dtype.
     Returns O [B, Hq, D] float32, LSE [B, Hq] float32."""
-    q, k, v = _as64(q), _as64(k), _as64(v)
     B, Hq, D = q.shape
     Hkv = k.shape[1]
     G = Hq // Hkv
@@ -130,11 +138,12 @@ def decode_reference(q, k, v, kv_lens, kv_offsets, scale):
     lse = np.empty((B, Hq), dtype=np.float32)
     for b in range(B):
         s0, L = int(kv_offsets[b]), int(kv_lens[b])
-        for hq in range(Hq):
-            hkv = hq // G
-            o, l = _row_attention(q[b, hq][None], k[s0 : s0 + L, hkv], v[s0 : s0 + L, hkv], scale)
-            out[b, hq] = o[0]
-            lse[b, hq] = l[0]
+        qb = _as64(q[b])
+        kb, vb = _as64(k[s0 : s0 + L]), _as64(v[s0 : s0 + L])
+        for hkv in range(Hkv):
+            o, l = _row_attention(qb[hkv * G : (hkv + 1) * G], kb[:, hkv], vb[:, hkv], scale)
+            out[b, hkv * G : (hkv + 1) * G] = o
+            lse[b, hkv * G : (hkv + 1) * G] = l
     return out, lse
 
 

@@ -137,3 +137,45 @@ def test_decode_paged(page_size, D):
     ro, rl = orc.decode_reference(q.float(), k, v, lens, offs, 1 / math.sqrt(D))
     assert np.abs(o.float().cpu().numpy() - ro).max() <= O_TOL
     assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL
+
+
+@pytest.mark.parametrize("entry", ["workspace", "static"])
+def test_decode_overlapping_offsets_overflow_is_reported(entry):
+    """Sequences that share rows through overlapping offsets can need more
+    partials than a workspace sized from total_tokens holds.  The call must not
+    read or write past the workspace: it writes empty rows (O = 0, LSE = -inf)
+    and reports BW_ERR_WORKSPACE; the next call on the stream is clean."""
+    import ctypes
+    import blackwell_b200 as bw
+    from blackwell_b200 import _ffi
+    lib = _ffi.lib()
+    B, Hq, Hkv, D, total, chunk = 4, 16, 2, 128, 4096, 64
+    q = seeded_bf16((B, Hq, D), 41).cuda()
+    k = seeded_bf16((total, Hkv, D), 42).cuda()
+    v = seeded_bf16((total, Hkv, D), 43).cuda()
+    lens = torch.full((B,), total, dtype=torch.int32, device="cuda")      # every sequence = all rows
+    offs = torch.zeros(B, dtype=torch.int64, device="cuda")
+    o = torch.full((B, Hq, D), 7.0, dtype=torch.bfloat16, device="cuda")
+    lse = torch.zeros(B, Hq, dtype=torch.float32, device="cuda")
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if entry == "workspace":
+        n = lib.bw_gqa_decode_workspace_size(B, Hq, Hkv, D, total, chunk)
+        guard = 1 << 20
+        ws = torch.full((n + guard,), 0xAB, dtype=torch.uint8, device="cuda")
+        rc = lib.bw_gqa_decode(P(q), P(k), P(v), P(lens), P(offs), P(o), P(lse), B, Hq, Hkv, D, total,
+                               1 / math.sqrt(D), chunk, P(ws), n, stream)
+    else:
+        rc = lib.bw_gqa_decode_static(P(q), P(k), P(v), P(lens), P(offs), P(o), P(lse), B, Hq, Hkv, D, total,
+                                      1 / math.sqrt(D), chunk, stream)
+    assert rc == 0
+    assert lib.bw_stream_status(stream) == _ffi.BW_ERR_WORKSPACE
+    assert torch.all(o == 0) and torch.all(torch.isneginf(lse))
+    if entry == "workspace":
+        assert torch.all(ws[n:] == 0xAB)          # nothing written past the workspace
+    # the same sequences without overlap fit and decode correctly afterwards
+    o2, l2, _ = _decode(q.cpu(), k.cpu(), v.cpu(), [1024, 1024, 1024, 1024])
+    ro, rl = orc.decode_reference(q.float().cpu(), k.float().cpu(), v.float().cpu(), [1024] * 4,
+                                  [0, 1024, 2048, 3072], 1 / math.sqrt(D))
+    assert np.abs(o2 - ro).max() <= O_TOL
+    assert np.abs(l2 - rl).max() <= LSE_TOL

@@ -39,3 +39,36 @@ def test_withheld_tile_reports_timeout_and_recovers(kernel, D):
     assert bw.stream_status() == 0
     ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float())
     assert (o.float() - ref).abs().max().item() < 2e-2
+
+
+def test_errors_are_per_stream():
+    """A call whose waits time out (withheld K tile) on one stream and a normal
+    call on another stream: each stream's status reports only its own call, and
+    reading one does not clear the other."""
+    import blackwell_b200 as bw
+    from blackwell_b200 import _ffi
+    q = seeded_bf16((1, 2, 256, 128), 4).cuda()
+    k = seeded_bf16((1, 2, 256, 128), 5).cuda()
+    v = seeded_bf16((1, 2, 256, 128), 6).cuda()
+    s_bad, s_good = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    old_t = bw.get_option(_ffi.BW_OPT_TIMEOUT_NS)
+    try:
+        bw.set_option(_ffi.BW_OPT_TIMEOUT_NS, 50_000_000)   # 50 ms
+        bw.set_option(_ffi.BW_OPT_DEBUG_FLAGS, 1)            # read at launch: only the next call withholds
+        with torch.cuda.stream(s_bad):
+            bw.mha_fwd(q, k, v)
+        bw.set_option(_ffi.BW_OPT_DEBUG_FLAGS, 0)
+        with torch.cuda.stream(s_good):
+            o, _ = bw.mha_fwd(q, k, v)
+        with torch.cuda.stream(s_good):
+            assert bw.stream_status() == _ffi.BW_OK
+        with torch.cuda.stream(s_bad):
+            assert bw.stream_status() == _ffi.BW_ERR_TIMEOUT
+            assert bw.stream_status() == _ffi.BW_OK          # read and cleared
+    finally:
+        bw.set_option(_ffi.BW_OPT_DEBUG_FLAGS, 0)
+        bw.set_option(_ffi.BW_OPT_TIMEOUT_NS, old_t)
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float())
+    assert (o.float() - ref).abs().max().item() < 2e-2

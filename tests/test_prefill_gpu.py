@@ -16,13 +16,12 @@ pytestmark = pytest.mark.gpu
 GOLDEN_GQA = ["gqa_nc_d128", "gqa_causal_d128", "gqa_causal_d64_g3_rand", "gqa_causal_d64_ragged", "gqa_split_d64"]
 
 
-@pytest.fixture(scope="module", params=[(4, 1), (3, 1), (2, 1), (1, 1), (1, 0)],
-                ids=["k4_one_acc", "k3_split_rows", "k2_dbuf", "k1_p_tmem", "k1_p_smem"])
+@pytest.fixture(scope="module", params=[(4, 1), (3, 1), (1, 1), (1, 0)],
+                ids=["k4_one_acc", "k3_split_rows", "k1_p_tmem", "k1_p_smem"])
 def p_variant(request):
     """Kernel variants: one query block with three score buffers and one
     accumulator, four threads per row (kernel 4); one query block with two
-    score buffers and rows split over two threads (kernel 3), 64-key tiles with two score buffers
-    (kernel 2), or two query blocks with P fed to the PV MMA from TMEM or
+    score buffers and rows split over two threads (kernel 3), or two query blocks with P fed to the PV MMA from TMEM or
     shared memory (kernel 1)."""
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
@@ -266,7 +265,7 @@ def test_mha_fp32_shapes(S):
     assert np.abs(lse.cpu().numpy() - rl).max() <= 5e-3  # TF32 logits
 
 
-@pytest.mark.parametrize("kernel", [4, 3, 1, 2])
+@pytest.mark.parametrize("kernel", [4, 3, 1])
 @pytest.mark.parametrize("q_scale,causal", [(12.0, True), (12.0, False), (0.02, True)])
 def test_logit_range_stress(kernel, q_scale, causal):
     """Large logits (q scaled up: the running max moves by far more than the
@@ -293,4 +292,4 @@ def test_logit_range_stress(kernel, q_scale, causal):
     lc = lse.cpu().numpy()[0][rows[:, 1], rows[:, 2]]
     assert np.isfinite(oc).all() and np.isfinite(lc).all()
     assert np.abs(oc - ro).max() <= O_TOL
-    assert np.abs(lc - rl).max() <= LSE_TOL * max(1.0, np.abs(rl).max() / 100)
+    assert np.abs(lc - rl).max() <= LSE_TOL

@@ -4,8 +4,9 @@ It exists for callers that cannot allocate device memory (allocator hooks,
 memory-pool callbacks, host runtimes that own no allocator): it keeps its
 scratch in a fixed array inside the library instead of a caller workspace.
 This test calls it through the C ABI twice in a row and checks each result
-against the workspace-taking bw_gqa_decode on the same inputs, within the
-parity tolerances the other tests use.  The file name sorts last so that a run
+against the workspace-taking bw_gqa_decode on the same inputs and against the
+fp64 oracle, within the parity tolerances the other tests use; after the first
+call (which does the set-up) the device's free memory must not change.  The file name sorts last so that a run
 stopping at the first failure has already run every other test; it also works
 alone in a fresh process (the first call does the per-device set-up)."""
 import ctypes
@@ -15,6 +16,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import attention_oracle as orc
 from tests._util import LSE_TOL, O_TOL, seeded_bf16
 
 pytestmark = pytest.mark.gpu
@@ -52,15 +54,24 @@ def test_static_scratch_decode_matches_workspace_decode():
                                Hkv, D, total, scale, chunk, _ptr(ws), ws.numel(), stream)
         assert rc == 0
         assert lib.bw_stream_status(stream) == 0
-        for _ in range(2):  # two calls in a row share (and reuse) the static scratch
-            o = torch.full((B, Hq, D), float("nan"), dtype=torch.bfloat16, device="cuda")
-            lse = torch.full((B, Hq), float("nan"), dtype=torch.float32, device="cuda")
+        ro, rl = orc.decode_reference(q, k, v, lens.cpu().numpy(), offs.cpu().numpy(), scale)
+        outs = [(torch.full((B, Hq, D), float("nan"), dtype=torch.bfloat16, device="cuda"),
+                 torch.full((B, Hq), float("nan"), dtype=torch.float32, device="cuda")) for _ in range(2)]
+        torch.cuda.synchronize()
+        free_before = None
+        for i, (o, lse) in enumerate(outs):  # two calls in a row share (and reuse) the static scratch
             rc = lib.bw_gqa_decode_static(_ptr(q), _ptr(k), _ptr(v), _ptr(lens), _ptr(offs), _ptr(o), _ptr(lse), B,
                                           Hq, Hkv, D, total, scale, chunk, stream)
             assert rc == 0
             assert lib.bw_stream_status(stream) == 0
+            if i == 0:
+                free_before = torch.cuda.mem_get_info()[0]
+            else:
+                assert torch.cuda.mem_get_info()[0] == free_before   # the call allocated nothing
             assert (o.float() - o_ref.float()).abs().max().item() <= O_TOL
             assert (lse - l_ref).abs().max().item() <= LSE_TOL
+            assert np.abs(o.float().cpu().numpy() - ro).max() <= O_TOL
+            assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL
 
 
 def test_static_scratch_rejects_oversize():
