@@ -160,6 +160,21 @@ def c2_config(world):
 
 
 # ---------------------------------------------------------------- CPU path
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def median_rate(work, times):
+    """work / median(seconds): the statistic both arms and every CPU leg use."""
+    return work / statistics.median(times)
+
+
 class CpuReference:
     """The reference's CPU path (torch SDPA, enable_gqa, causal) on one (b, KV-group)
     slice of C2: G=4 query heads x S=4096 x D=128, bf16, all host cores."""
@@ -184,15 +199,74 @@ class CpuReference:
         self.fn(self.q, self.k, self.v, self.scale, causal=True)
         return time.perf_counter() - t0
 
-    def measure(self, budget_s=10.0, max_reps=200):
-        self.step()
+    def measure(self, warmup=3, budget_s=10.0, max_reps=200, min_reps=5):
+        for _ in range(warmup):
+            self.step()
         times = []
         t_end = time.perf_counter() + budget_s
-        while not times or (time.perf_counter() < t_end and len(times) < max_reps):
+        while len(times) < min_reps or (time.perf_counter() < t_end and len(times) < max_reps):
             times.append(self.step())
-        t = statistics.median(times)
-        return {"value": self.flops / t / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                "kind": "port", "sample": self.sample + f", median of {len(times)}"}
+        return self.summary(times)
+
+    def summary(self, times):
+        return {"value": median_rate(self.flops, times) / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                "kind": "port", "stat": f"median of {len(times)} samples after warm-up", "cpu_model": cpu_model(),
+                "sample": self.sample}
+
+
+def cpu_legs(budget_s=4.0):
+    """The other configurations' CPU path (the reference's torch SDPA calls) on
+    bounded samples, reported in each configuration's own unit:
+
+    * C4 decode: the per-sequence SDPA loop (Sq = 1, enable_gqa) over the first
+      4 of the 64 seeded sequences, as K/V bytes read per second (GB/s);
+    * C3 MHA D=128: one (b, h) slice of the non-causal B=8 H=16 S=2048 call;
+    * C5 long context: one KV group (8 query heads) at S=16384, causal,
+      EXTRAPOLATED to S=131072 by the S^2 work ratio (the full slice would take
+      minutes per sample)."""
+    from oracle.attention_oracle import sdpa_cpu
+    torch.set_num_threads(os.cpu_count() or 1)
+
+    def timed(fn):
+        fn()
+        times, t_end = [], time.perf_counter() + budget_s
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+        return times
+
+    legs = {}
+    lens = torch.randint(1024, 32769, (64,), generator=torch.Generator().manual_seed(42))[:4].tolist()
+    g = torch.Generator().manual_seed(42)
+    Hq, Hkv, D = 64, 8, 128
+    q = torch.randn(4, Hq, 1, D, generator=g).bfloat16()
+    kv = [(torch.randn(1, Hkv, L, D, generator=g).bfloat16(), torch.randn(1, Hkv, L, D, generator=g).bfloat16())
+          for L in lens]
+    t = timed(lambda: [sdpa_cpu(q[b:b + 1], k, v, 1 / math.sqrt(D)) for b, (k, v) in enumerate(kv)])
+    nbytes = sum(2 * L * Hkv * D * 2 for L in lens)
+    legs["C4_decode"] = {"value": median_rate(nbytes, t) / 1e9, "unit": "GB/s",
+                         "sample": f"per-sequence SDPA loop over 4 of the 64 C4 sequences (L = {lens})",
+                         "stat": f"median of {len(t)}"}
+    S = 2048
+    q3 = torch.randn(1, 1, S, D, generator=g).bfloat16()
+    k3 = torch.randn(1, 1, S, D, generator=g).bfloat16()
+    v3 = torch.randn(1, 1, S, D, generator=g).bfloat16()
+    t = timed(lambda: sdpa_cpu(q3, k3, v3, 1 / math.sqrt(D)))
+    legs["C3_mha_D128"] = {"value": median_rate(4.0 * S * S * D, t) / 1e12, "unit": "TFLOP/s",
+                           "sample": "one (b, h) slice of C3 D=128 (S=2048, non-causal)", "stat": f"median of {len(t)}"}
+    S5 = 16384
+    q5 = torch.randn(1, 8, S5, D, generator=g).bfloat16()
+    k5 = torch.randn(1, 1, S5, D, generator=g).bfloat16()
+    v5 = torch.randn(1, 1, S5, D, generator=g).bfloat16()
+    t = timed(lambda: sdpa_cpu(q5, k5, v5, 1 / math.sqrt(D), causal=True))
+    rate = median_rate(causal_flops(1, 8, S5, D), t)
+    full_s = causal_flops(1, 64, 131072, D) / rate
+    legs["C5_long_context"] = {"value": rate / 1e12, "unit": "TFLOP/s", "extrapolated": True,
+                               "ms_full_config_extrapolated": full_s * 1e3,
+                               "sample": "one KV group (8 query heads) causal at S=16384; full C5 time extrapolated "
+                                         "by the S^2 work ratio", "stat": f"median of {len(t)}"}
+    return legs
 
 
 def run_reference(args, world, rank):
@@ -202,11 +276,10 @@ def run_reference(args, world, rank):
     for _ in range(args.warmup):
         ref.step()
     t = [ref.step() for _ in range(args.steps)]
-    value = ref.flops * len(t) / sum(t) / 1e12
-    cpu = {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-           "sample": ref.sample}
+    cpu = ref.summary(t)
+    value = cpu["value"]
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(t) / len(t),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(t),
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1), seed 42", "scaling": "weak",
             "config": dict(c2_config(world), cpu_sample=ref.sample),
             "cpu_baseline": cpu,
@@ -304,6 +377,75 @@ def bench_decode_paged(flush, steps, warmup, page_size=64):
     del kc, vc
     return {"workload": f"C4 over a paged KV cache, page_size {page_size}, pages in random order",
             "ms": t, "GB/s": nbytes / t / 1e6}
+
+
+def bench_decode_sp(world, rank, steps, warmup, flush):
+    """C4 decode with every sequence's keys split over the ranks (sequence
+    parallel): per step each rank runs bw_gqa_decode_partial on its 1/N of every
+    sequence, ONE all-gather of the packed (O, LSE) partials over NCCL, and
+    bw_lse_combine_packed.  The three phases are timed separately with CUDA
+    events on the launching stream; each figure is the max over ranks of the
+    per-rank median."""
+    import blackwell_b200 as bw
+    from blackwell_b200.distributed import split_sequences
+    B, Hq, Hkv, D = 64, 64, 8, 128
+    lens = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(42))
+    loc, _ = split_sequences(lens.numpy(), world, rank)
+    loc_t = torch.from_numpy(loc)
+    total = int(loc_t.sum())
+    offs = (torch.cumsum(loc_t.long(), 0) - loc_t.long())
+    g = torch.Generator(device="cuda").manual_seed(42)
+    q = torch.randn(B, Hq, D, generator=g, device="cuda").bfloat16()
+    g.manual_seed(1000 + rank)
+    k = torch.randn(total, Hkv, D, generator=g, device="cuda").bfloat16()
+    v = torch.randn(total, Hkv, D, generator=g, device="cuda").bfloat16()
+    lens_d, offs_d = loc_t.int().cuda(), offs.cuda()
+    ws = torch.empty(bw.attention.decode_workspace_size(B, Hq, Hkv, D, total), dtype=torch.uint8, device="cuda")
+    P = bw.attention.packed_split_floats(B, Hq, D)
+    n_o = B * Hq * D
+    buf = torch.empty(P, dtype=torch.float32, device="cuda")
+    gathered = torch.empty(world, P, dtype=torch.float32, device="cuda")
+    o = torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, Hq, dtype=torch.float32, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+
+    def step(e=None):
+        if e: e[0].record()
+        bw.attention.gqa_decode_partial(q, k, v, lens_d, offs_d, workspace=ws, out=buf[:n_o].view(B, Hq, D),
+                                        lse=buf[n_o:n_o + B * Hq].view(B, Hq))
+        if e: e[1].record()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, buf)
+        else:
+            gathered[0].copy_(buf)
+        if e: e[2].record()
+        bw.attention.lse_combine_packed(gathered, B, Hq, D, out=o, lse=lse)
+        if e: e[3].record()
+
+    for _ in range(warmup):
+        flush()
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    for e in ev:
+        flush()
+        step(e)
+    torch.cuda.synchronize()
+    barrier(world)
+    assert bw.stream_status() == 0
+    med = lambda a, b: statistics.median(e[a].elapsed_time(e[b]) for e in ev)
+    r = {ph: max_over_ranks(med(a, b), world) for ph, (a, b) in
+         {"ms_decode_partial": (0, 1), "ms_allgather": (1, 2), "ms_combine": (2, 3), "ms": (0, 3)}.items()}
+    full_total = int(lens.sum())
+    nbytes = 2 * full_total * Hkv * D * 2 + 2 * B * Hq * D * 2 + B * Hq * 4
+    r.update({"workload": "C4 decode, every sequence's keys split over the ranks (sequence parallel), "
+                          "one NCCL all-gather of packed (O, LSE) partials + LSE-combine",
+              "ranks": world, "bytes_allgathered_per_rank": P * 4, "GB/s_total": nbytes / r["ms"] / 1e6,
+              "GB/s_per_gpu": nbytes / r["ms"] / 1e6 / world})
+    del k, v
+    return r
 
 
 def bench_prefill(shape, causal, layout, flush, steps, warmup):
@@ -477,13 +619,21 @@ def run_ours(args, world, rank, local):
 
     if not (args.no_secondary or args.profile):
         c5 = bench_c5(world, rank, 3, 3)
+        sp = bench_decode_sp(world, rank, 20, 3, flush)
         if rank == 0:
-            c5["frac_of_peak_per_gpu"] = c5["TFLOP/s_per_gpu"] / peaks["bf16_tflops"]
+            # a quarter-second launch is a sustained load: its fraction is quoted
+            # against the sustained peak (the burst one beside it)
+            sus = peaks.get("bf16_tflops_sustained")
+            c5["frac_of_sustained_peak_per_gpu"] = c5["TFLOP/s_per_gpu"] / sus if sus else None
+            c5["frac_of_burst_peak_per_gpu"] = c5["TFLOP/s_per_gpu"] / peaks["bf16_tflops"]
             secondary["C5_long_context"] = c5
+            sp["frac_of_hbm_peak_per_gpu"] = sp["GB/s_per_gpu"] / peaks["hbm_gbs"]
+            secondary["C4_decode_sequence_parallel"] = sp
 
     cpu = None
     if rank == 0 and world == 1 and not args.profile:
-        cpu = CpuReference().measure(budget_s=10.0)
+        cpu = CpuReference().measure(warmup=3, budget_s=10.0)
+        cpu["legs"] = cpu_legs()
 
     if rank == 0:
         line = {

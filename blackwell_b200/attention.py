@@ -368,8 +368,9 @@ def attention_from_host(q_host, k_host, v_host, o_host, lse_host=None, scale=Non
 
 
 def mha_fwd_f32(q, k, v, scale=None, out=None, lse=None):
-    """fp32 MHA forward (the reference's mha_v3_tc data types: fp32 in / out), D = 64;
-    Q K^T on TF32 tensor cores, P V in bf16 (V rounded to bf16 in a workspace):
+    """fp32 MHA forward at fp32 accuracy (the reference's mha_v3_tc: fp32 in / out
+    and its 3xTF32 split), D = 64: Q K^T and P V each as three TF32 tensor-core
+    products of hi / lo parts (split into a workspace):
     q, k, v [B, H, S, 64] float32 CUDA views with contiguous D.  Returns (O fp32, LSE)."""
     for name, t in (("q", q), ("k", k), ("v", v)):
         if not t.is_cuda or t.dtype != torch.float32 or t.dim() != 4 or t.stride(3) != 1:

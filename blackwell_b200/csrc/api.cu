@@ -277,17 +277,19 @@ int bw_mha_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE,
 
 size_t bw_mha_f32_workspace_size(int B, int H, int S, int D) {
   if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
-  return (size_t)B * H * S * D * 2;
+  const size_t rows = align256((size_t)B * H * S * D * 4);
+  const size_t vt = align256((size_t)B * H * D * (((size_t)S + 31) & ~size_t(31)) * 4);
+  return 4 * rows + 2 * vt;
 }
 
 int bw_mha_fwd_f32(const float* Q, const float* K, const float* V, float* O, float* LSE, int B, int H, int S, int D,
                    float scale, const bw_strides* strides, void* workspace, size_t workspace_bytes, void* stream) {
   if (!Q || !K || !V || !O || !workspace) return BW_ERR_NULL;
-  if (workspace_bytes < bw_mha_f32_workspace_size(B, H, S, D)) return BW_ERR_WORKSPACE;
-  if (!aligned16(workspace)) return BW_ERR_ALIGN;
   if (B <= 0 || H <= 0 || S <= 0 || D != 64) return BW_ERR_SHAPE;
+  if (workspace_bytes < bw_mha_f32_workspace_size(B, H, S, D)) return BW_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return BW_ERR_ALIGN;
   if (!(scale > 0.f) || !std::isfinite(scale)) return BW_ERR_SHAPE;
-  if ((int64_t)B * H * ((S + 255) / 256) >= (int64_t(1) << 30)) return BW_ERR_SHAPE;
+  if ((int64_t)B * H * ((S + 127) / 128) >= (int64_t(1) << 31) || (int64_t)B * H > 65535) return BW_ERR_SHAPE;
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return BW_ERR_ALIGN;
   bw_strides st;
   if (strides) {
@@ -304,42 +306,50 @@ int bw_mha_fwd_f32(const float* Q, const float* K, const float* V, float* O, flo
   DeviceState* dev = nullptr;
   int rc = get_device_state(&dev);
   if (rc != BW_OK) return rc;
-  bw::FmhaMaps maps;
-  if (make_map_bhsd(&maps.q, Q, B, H, S, D, st.q, 128, true) != BW_OK) return BW_ERR_CUDA;
-  if (make_map_bhsd(&maps.k, K, B, H, S, D, st.k, 128, true) != BW_OK) return BW_ERR_CUDA;
-  // V -> bf16 (contiguous BHSD) in the workspace; the PV MMA runs on bf16 P and V
-  if (bw::launch_f32_to_bf16(V, st.v[0], st.v[1], st.v[2], workspace, B, H, S, D, dev->num_sms,
-                             static_cast<cudaStream_t>(stream)) != cudaSuccess)
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 3xTF32 split: Q, K hi / lo row-major, V hi / lo transposed, in the workspace
+  const int S32 = (S + 31) & ~31;
+  const size_t rows = align256((size_t)B * H * S * D * 4);
+  const size_t vtb = align256((size_t)B * H * D * S32 * 4);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* qh = reinterpret_cast<float*>(ws);
+  float* ql = reinterpret_cast<float*>(ws + rows);
+  float* kh = reinterpret_cast<float*>(ws + 2 * rows);
+  float* kl = reinterpret_cast<float*>(ws + 3 * rows);
+  float* vth = reinterpret_cast<float*>(ws + 4 * rows);
+  float* vtl = reinterpret_cast<float*>(ws + 4 * rows + vtb);
+  if (bw::launch_f32x3_split(Q, st.q[0], st.q[1], st.q[2], qh, ql, B, H, S, dev->num_sms, s) != cudaSuccess ||
+      bw::launch_f32x3_split(K, st.k[0], st.k[1], st.k[2], kh, kl, B, H, S, dev->num_sms, s) != cudaSuccess ||
+      bw::launch_f32x3_split_vt(V, st.v[0], st.v[1], st.v[2], vth, vtl, B, H, S, S32, s) != cudaSuccess)
     return BW_ERR_CUDA;
-  int64_t vst[3];
-  contiguous(H, S, D, vst);
-  if (make_map_bhsd(&maps.v, workspace, B, H, S, D, vst, 128, false) != BW_OK) return BW_ERR_CUDA;
-  bw::FmhaParams p{};
+  bw::F32x3Maps maps;
+  auto map = [&](CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint32_t b1) {
+    cuuint64_t dims[4] = {d0, d1, (cuuint64_t)H, (cuuint64_t)B};
+    cuuint64_t str[3] = {d0 * 4, d0 * d1 * 4, d0 * d1 * H * 4};
+    cuuint32_t box[4] = {32, b1, 1, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, str, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
+  if (!map(&maps.q_hi, qh, D, S, 128) || !map(&maps.q_lo, ql, D, S, 128) || !map(&maps.k_hi, kh, D, S, 32) ||
+      !map(&maps.k_lo, kl, D, S, 32) || !map(&maps.vt_hi, vth, S32, D, 64) || !map(&maps.vt_lo, vtl, S32, D, 64))
+    return BW_ERR_CUDA;
+  bw::F32x3Params p{};
   p.O = O;
   p.o_sb = st.o[0];
   p.o_sh = st.o[1];
   p.o_ss = st.o[2];
   p.LSE = LSE;
   p.B = B;
-  p.Hq = H;
-  p.Hkv = H;
-  p.G = 1;
-  p.Sq = S;
-  p.Skv = S;
-  p.D = D;
-  p.causal = 0;
-  p.scale_log2 = scale * 1.4426950408889634f;
+  p.H = H;
+  p.S = S;
   p.n_qtiles = (S + 127) / 128;
-  p.n_kvtiles = (S + 127) / 128;
-  p.pair_heads = 0;
-  p.num_items = B * H * ((p.n_qtiles + 1) / 2);
+  p.n_kvtiles = (S + 31) / 32;
+  p.scale_log2 = scale * 1.4426950408889634f;
   p.err = err_slot(dev, stream);
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
-  p.debug_flags = 0;
-  p.q_offset = 0;
-  p.lse_sh = S;
-  cudaError_t e = bw::launch_fmha_fwd_f32(p, maps, dev->num_sms, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
+  return bw::launch_fmha_f32x3(p, maps, s) == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
 size_t bw_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int64_t total_tokens, int chunk) {

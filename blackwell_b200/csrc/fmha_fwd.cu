@@ -39,26 +39,25 @@ namespace {
 constexpr int kRows = 128;          // query rows per block == KV rows per tile
 constexpr int kSmemBudget = 232448 - 2048;
 
-// EB: element bytes, 2 (bf16 operands, kind::f16) or 4 (fp32 operands, kind::tf32).
-template <int D, int EB>
+template <int D>
 struct Cfg {
-  static constexpr int kRowBytes = D * EB;
+  static constexpr int kRowBytes = D * 2;
   static constexpr int kTileBytes = kRows * kRowBytes;      // one 128-row tile
   static constexpr int kSub = kRows * 128;                  // one 128-byte swizzle panel
   static constexpr int kPanels = kRowBytes / 128;
-  static constexpr int kPanelElems = 128 / EB;              // elements per panel row
-  static constexpr int kPBytes = kRows * kRows * 2;         // P tile (smem variant, bf16 only)
-  static constexpr int kKStep = 32 / EB;                    // MMA K per instruction (32 bytes)
+  static constexpr int kPanelElems = 64;                    // elements per panel row
+  static constexpr int kPBytes = kRows * kRows * 2;         // P tile (smem variant)
+  static constexpr int kKStep = 16;                         // MMA K per instruction (32 bytes)
 };
 
-template <int D, bool PT, int EB = 2>
+template <int D, bool PT>
 struct Layout {
   static constexpr int kQ = 0;
-  static constexpr int kP = 2 * Cfg<D, EB>::kTileBytes;
-  static constexpr int kKV = kP + (PT ? 0 : 2 * Cfg<D, EB>::kPBytes);
-  static constexpr int kNSraw = (kSmemBudget - kKV) / Cfg<D, EB>::kTileBytes;
+  static constexpr int kP = 2 * Cfg<D>::kTileBytes;
+  static constexpr int kKV = kP + (PT ? 0 : 2 * Cfg<D>::kPBytes);
+  static constexpr int kNSraw = (kSmemBudget - kKV) / Cfg<D>::kTileBytes;
   static constexpr int NS = kNSraw > 8 ? 8 : kNSraw;
-  static constexpr int kBar = kKV + NS * Cfg<D, EB>::kTileBytes;
+  static constexpr int kBar = kKV + NS * Cfg<D>::kTileBytes;
   static constexpr int kBytes = kBar + 512;
   static_assert(NS >= 3, "K/V ring needs at least 3 slots");
 };
@@ -123,14 +122,14 @@ __device__ __forceinline__ Item decode_item(const FmhaParams& p, int idx) {
 }
 
 // ------------------------------------------------------------ producer warp
-template <int D, bool PT, int EB>
+template <int D, bool PT>
 __device__ void producer_role(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars& bars,
                               const WaitCtl& wc) {
-  using L = Layout<D, PT, EB>;
+  using L = Layout<D, PT>;
   constexpr int NS = L::NS;
-  constexpr int TB = Cfg<D, EB>::kTileBytes;
-  constexpr int NPANEL = Cfg<D, EB>::kPanels;
-  constexpr int PE = Cfg<D, EB>::kPanelElems;
+  constexpr int TB = Cfg<D>::kTileBytes;
+  constexpr int NPANEL = Cfg<D>::kPanels;
+  constexpr int PE = Cfg<D>::kPanelElems;
   uint32_t ld = 0;                 // K/V loads issued (ring position)
   uint32_t qc[2] = {0, 0};
   uint32_t armed = 0;              // bit s: slot s has a load whose completion is pending/known
@@ -146,7 +145,7 @@ __device__ void producer_role(const FmhaParams& p, const FmhaMaps& maps, uint8_t
       uint8_t* dst = smem + L::kQ + w * TB;
 #pragma unroll
       for (int c = 0; c < NPANEL; ++c)
-        tma_load_4d(dst + c * Cfg<D, EB>::kSub, &maps.q, &bars.q_full[w], c * PE, it.qt[w] * kRows, it.head[w], it.b);
+        tma_load_4d(dst + c * Cfg<D>::kSub, &maps.q, &bars.q_full[w], c * PE, it.qt[w] * kRows, it.head[w], it.b);
       ++qc[w];
     }
     for (int j = 0; ok && j < it.nmax; ++j) {
@@ -160,15 +159,13 @@ __device__ void producer_role(const FmhaParams& p, const FmhaMaps& maps, uint8_t
         const bool withhold = kind == 0 && first_k && (p.debug_flags & 1);
         if (kind == 0) first_k = false;
         if (!withhold) {
-          // K has the operand element size EB; V is always bf16 (the fp32 path
-          // converts V beforehand), i.e. D / 64 panels of 64 elements.
-          const int np = kind == 0 ? NPANEL : D / 64;
-          const int pe = kind == 0 ? PE : 64;
-          mbar_arrive_expect_tx(&bars.kv_full[slot], kind == 0 ? TB : kRows * D * 2);
+          const int np = NPANEL;
+          const int pe = PE;
+          mbar_arrive_expect_tx(&bars.kv_full[slot], TB);
           uint8_t* dst = smem + L::kKV + slot * TB;
           const CUtensorMap* m = kind == 0 ? &maps.k : &maps.v;
           for (int c = 0; c < np; ++c)
-            tma_load_4d(dst + c * Cfg<D, EB>::kSub, m, &bars.kv_full[slot], c * pe, j * kRows, it.kvh, it.b);
+            tma_load_4d(dst + c * Cfg<D>::kSub, m, &bars.kv_full[slot], c * pe, j * kRows, it.kvh, it.b);
           armed |= 1u << slot;
         } else {
           armed &= ~(1u << slot);
@@ -194,16 +191,15 @@ __device__ void producer_role(const FmhaParams& p, const FmhaMaps& maps, uint8_t
 // tcgen05 operations from one thread execute in issue order, so the commit that
 // signals S_w(j+1) ready also guarantees PV_w(j) has finished reading P_w(j)
 // (which shares S_w's columns) and that O_w is stable for the softmax's rescale.
-template <int D, bool PT, int EB>
+template <int D, bool PT>
 __device__ void mma_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const WaitCtl& wc, uint32_t tmem) {
-  using L = Layout<D, PT, EB>;
+  using L = Layout<D, PT>;
   constexpr int NS = L::NS;
-  constexpr int TB = Cfg<D, EB>::kTileBytes;
-  constexpr int SUB = Cfg<D, EB>::kSub;
-  constexpr bool F32 = EB == 4;
-  constexpr uint32_t IDESC_QK = F32 ? idesc_tf32_f32(128, 128, false) : idesc_bf16_f32(128, 128, false);
-  constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, true);   // P and V are bf16 in every variant
-  constexpr int KS = Cfg<D, EB>::kKStep;
+  constexpr int TB = Cfg<D>::kTileBytes;
+  constexpr int SUB = Cfg<D>::kSub;
+  constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 128, false);
+  constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, true);
+  constexpr int KS = Cfg<D>::kKStep;
   const uint32_t smem_base = smem_u32(smem);
   uint32_t ld = 0;
   uint32_t qc[2] = {0, 0}, pc[2] = {0, 0};
@@ -224,10 +220,7 @@ __device__ void mma_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const W
 #pragma unroll
     for (int ks = 0; ks < D / KS; ++ks) {
       const uint32_t off = ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
-      if constexpr (F32)
-        mma_ss_lh_tf32(d_tmem, qa + off, HI, ka + off, HI, IDESC_QK, ks > 0);
-      else
-        mma_ss_lh(d_tmem, qa + off, HI, ka + off, HI, IDESC_QK, ks > 0);
+      mma_ss_lh(d_tmem, qa + off, HI, ka + off, HI, IDESC_QK, ks > 0);
     }
   };
   auto issue_pv = [&](int w, uint32_t vslot, bool acc) {
@@ -240,7 +233,7 @@ __device__ void mma_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const W
       if constexpr (PT) {
         mma_ts_lh(o_tmem, tmem + w * 128 + ks * 8, b_lo, HI, IDESC_PV, ks > 0 ? 1u : acc0);
       } else {
-        const uint32_t pa = p_lo0 + (uint32_t)(w * Cfg<D, EB>::kPBytes) / 16 + ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
+        const uint32_t pa = p_lo0 + (uint32_t)(w * Cfg<D>::kPBytes) / 16 + ((ks >> 2) * SUB + (ks & 3) * 32) / 16;
         mma_ss_lh(o_tmem, pa, HI, b_lo, HI, IDESC_PV, ks > 0 ? 1u : acc0);
       }
     }
@@ -308,17 +301,17 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 // ----------------------------------------------------------- softmax warpgroups
 // Thread t of warpgroup w owns query row t of block w (TMEM lane t).
-template <int D, bool PT, int POLY, int EB>
+template <int D, bool PT, int POLY>
 __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, const WaitCtl& wc, uint32_t tmem,
                              int w, int t) {
-  using L = Layout<D, PT, EB>;
+  using L = Layout<D, PT>;
   const int wq = t >> 5;                                 // warp within warpgroup -> lane quarter
   const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
   const uint32_t s_tmem = tmem + lane_off + w * 128;
   const uint32_t o_tmem = tmem + lane_off + 256 + w * D;
   const float c = p.scale_log2;
   uint32_t sc = 0, oc = 0;
-  uint8_t* p_smem = smem + L::kP + w * Cfg<D, EB>::kPBytes;
+  uint8_t* p_smem = smem + L::kP + w * Cfg<D>::kPBytes;
 
   for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
     const Item it = decode_item(p, idx);
@@ -412,7 +405,7 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
         for (int ch = 0; ch < 16; ++ch) {
           const int panel = ch >> 3, cc = ch & 7;
           uint4 v = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-          *reinterpret_cast<uint4*>(p_smem + panel * Cfg<D, EB>::kSub + t * 128 + ((cc ^ (t & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(p_smem + panel * Cfg<D>::kSub + t * 128 + ((cc ^ (t & 7)) << 4)) = v;
         }
       }
       if (j > 0 && __any_sync(0xffffffffu, upd)) {
@@ -436,24 +429,9 @@ __device__ void softmax_role(const FmhaParams& p, uint8_t* smem, Bars& bars, con
     tc_fence_after();
     const float inv_l = 1.f / l_run;
     const int h = it.head[w];
-    if constexpr (EB == 4) {
-      float* orow32 = reinterpret_cast<float*>(p.O) + it.b * p.o_sb + h * p.o_sh + (int64_t)row * p.o_ss;
-#pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        tmem_ld32(o_tmem + c0, o);
-        if (row < p.Sq) {
-          float4* dst = reinterpret_cast<float4*>(orow32 + c0);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
-                                 __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
-        }
-      }
-    }
     __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.O) + it.b * p.o_sb + h * p.o_sh + (int64_t)row * p.o_ss;
 #pragma unroll
-    for (int c0 = 0; c0 < (EB == 4 ? 0 : D); c0 += 32) {
+    for (int c0 = 0; c0 < D; c0 += 32) {
       uint32_t o[32];
       tmem_ld32(o_tmem + c0, o);
       uint32_t q[16];
@@ -479,10 +457,10 @@ struct Roles {
   static constexpr int kThreads = 32 * (kMmaWarp + 1);
 };
 
-template <int D, bool PT, int POLY, int EB>
+template <int D, bool PT, int POLY>
 __global__ void __launch_bounds__(Roles::kThreads, 1)
     fmha_fwd_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
-  using L = Layout<D, PT, EB>;
+  using L = Layout<D, PT>;
   using R = Roles;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -521,11 +499,11 @@ __global__ void __launch_bounds__(Roles::kThreads, 1)
 
   if (warp < R::kProducerWarp) {
     const int w = tid / R::kSoftThreads;
-    softmax_role<D, PT, POLY, EB>(p, smem, bars, wc, tmem, w, tid % R::kSoftThreads);
+    softmax_role<D, PT, POLY>(p, smem, bars, wc, tmem, w, tid % R::kSoftThreads);
   } else if (warp == R::kProducerWarp) {
-    if (lane == 0) producer_role<D, PT, EB>(p, maps, smem, bars, wc);
+    if (lane == 0) producer_role<D, PT>(p, maps, smem, bars, wc);
   } else {
-    if (lane == 0) mma_role<D, PT, EB>(p, smem, bars, wc, tmem);
+    if (lane == 0) mma_role<D, PT>(p, smem, bars, wc, tmem);
   }
   tc_fence_before();
   __syncthreads();
@@ -535,11 +513,11 @@ __global__ void __launch_bounds__(Roles::kThreads, 1)
   }
 }
 
-template <int D, bool PT, int POLY, int EB = 2>
+template <int D, bool PT, int POLY>
 cudaError_t launch_impl(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
-  constexpr int bytes = Layout<D, PT, EB>::kBytes + 1024;
+  constexpr int bytes = Layout<D, PT>::kBytes + 1024;
   constexpr int kThreads = Roles::kThreads;
-  auto kern = fmha_fwd_kernel<D, PT, POLY, EB>;
+  auto kern = fmha_fwd_kernel<D, PT, POLY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
   const int grid = p.num_items < num_sms ? p.num_items : num_sms;
@@ -559,11 +537,6 @@ cudaError_t launch_poly(const FmhaParams& p, const FmhaMaps& maps, int poly, int
 }
 
 }  // namespace
-
-cudaError_t launch_fmha_fwd_f32(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
-  if (p.D == 64) return launch_impl<64, true, 2, 4>(p, maps, num_sms, stream);
-  return cudaErrorInvalidValue;
-}
 
 cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int exp_poly, int num_sms,
                             cudaStream_t stream) {

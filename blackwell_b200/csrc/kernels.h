@@ -41,14 +41,30 @@ struct FmhaMaps {
 cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int exp_poly, int num_sms,
                             cudaStream_t stream);
 
-// fp32 Q, K and output: QK^T with kind::tf32 MMAs; P (bf16 in TMEM) times V
-// (bf16, converted beforehand) with kind::f16; D = 64.  maps.q / maps.k are
-// FLOAT32 with 32-element, 128-row boxes, maps.v bf16 as usual; O is fp32.
-cudaError_t launch_fmha_fwd_f32(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream);
-
-// fp32 -> bf16 copy of a [B, H, S, D] tensor (contiguous destination).
-cudaError_t launch_f32_to_bf16(const float* src, int64_t sb, int64_t sh, int64_t ss, void* dst, int B, int H, int S,
-                               int D, int num_sms, cudaStream_t stream);
+// fp32 MHA at fp32 accuracy (3xTF32 split, D = 64): split passes and the
+// attention kernel (fmha_f32x3.cu).  The split arrays: Q and K hi / lo as
+// contiguous [B, H, S, 64] fp32, V hi / lo transposed [B, H, 64, S32] fp32
+// (S32 = S rounded up to 32, zero columns past S).
+struct F32x3Params {
+  float* O;                      // fp32, element strides below (d stride 1)
+  int64_t o_sb, o_sh, o_ss;
+  float* LSE;                    // fp32 [B, H, S] or null
+  int B, H, S;
+  int n_qtiles, n_kvtiles;       // ceil(S / 128), ceil(S / 32)
+  float scale_log2;
+  int* err;
+  uint64_t timeout_ns;
+};
+struct F32x3Maps {
+  // fp32, SWIZZLE_128B, 32-element (128-byte) inner box: Q (64, S, H, B) box
+  // (32, 128); K (64, S, H, B) box (32, 32); VT (S32, 64, H, B) box (32, 64)
+  CUtensorMap q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo;
+};
+cudaError_t launch_f32x3_split(const float* x, int64_t sb, int64_t sh, int64_t ss, float* hi, float* lo, int B,
+                               int H, int S, int num_sms, cudaStream_t stream);
+cudaError_t launch_f32x3_split_vt(const float* x, int64_t sb, int64_t sh, int64_t ss, float* hi, float* lo, int B,
+                                  int H, int S, int S32, cudaStream_t stream);
+cudaError_t launch_fmha_f32x3(const F32x3Params& p, const F32x3Maps& maps, cudaStream_t stream);
 
 // One query tile per work item, double-buffered scores (one softmax warpgroup).
 cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,

@@ -143,37 +143,8 @@ __global__ void __launch_bounds__(256, kMinBlocks) norm_rope_kernel(const NormRo
   }
 }
 
-// fp32 -> bf16 (round to nearest even), 4 elements per thread, grid-stride.
-__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* src, int64_t sb, int64_t sh, int64_t ss,
-                                                          __nv_bfloat16* dst, int B, int H, int S, int D) {
-  const int64_t quads = (int64_t)B * H * S * D / 4;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t e = i * 4;
-    const int d = (int)(e % D);
-    const int64_t r = e / D;
-    const int s = (int)(r % S);
-    const int64_t bh = r / S;
-    const int h = (int)(bh % H), b = (int)(bh / H);
-    const float4 v = *reinterpret_cast<const float4*>(src + b * sb + h * sh + (int64_t)s * ss + d);
-    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-    uint2 u;
-    u.x = *reinterpret_cast<uint32_t*>(&lo);
-    u.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(dst + e) = u;
-  }
-}
-
 }  // namespace
 
-cudaError_t launch_f32_to_bf16(const float* src, int64_t sb, int64_t sh, int64_t ss, void* dst, int B, int H, int S,
-                               int D, int num_sms, cudaStream_t stream) {
-  const int64_t quads = (int64_t)B * H * S * D / 4;
-  if (quads == 0) return cudaSuccess;
-  int64_t blocks = (quads + 255) / 256;
-  if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
-  f32_to_bf16_kernel<<<(int)blocks, 256, 0, stream>>>(src, sb, sh, ss, static_cast<__nv_bfloat16*>(dst), B, H, S, D);
-  return cudaGetLastError();
-}
 
 cudaError_t launch_norm_rope(const NormRopeParams& p, int num_sms, cudaStream_t stream) {
   const int64_t rows = (int64_t)p.B * p.H * p.S;

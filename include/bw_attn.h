@@ -97,11 +97,13 @@ BW_API int bw_gqa_causal_offset_fwd(const void* Q, const void* K, const void* V,
 BW_API int bw_mha_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, int B, int H, int S, int D,
                float scale, const bw_strides* strides, void* stream);
 
-/* MHA forward with fp32 inputs and output, the data types of the reference's
- * mha_v3_tc (src/SM120/attention/MHA_sm120.cu:64-71, fp32 via a 3-way TF32
- * split).  Here Q K^T runs as kind::tf32 MMAs (10-bit mantissa inputs, fp32
- * accumulation: logits to ~1e-3 relative) and P V as bf16 MMAs on V rounded to
- * bf16 in `workspace` (bw_mha_f32_workspace_size bytes); O is fp32; D = 64; LSE
+/* MHA forward with fp32 inputs and output at fp32 accuracy: the data types and
+ * the 3xTF32 split of the reference's mha_v3_tc
+ * (src/SM120/attention/MHA_sm120.cu:64-71; split_tf32 :39-62 applied to Q, K
+ * and V :119-138).  Each operand is split into TF32 hi / lo parts (written to
+ * `workspace`, bw_mha_f32_workspace_size bytes, 256-byte aligned) and
+ * Q K^T and P V each run as three kind::tf32 tensor-core products
+ * (hi*hi + hi*lo + lo*hi); softmax, sums and O / l in fp32.  D = 64; LSE
  * optional.  Strides are fp32 element strides (multiples of 4). */
 BW_API size_t bw_mha_f32_workspace_size(int B, int H, int S, int D);
 BW_API int bw_mha_fwd_f32(const float* Q, const float* K, const float* V, float* O, float* LSE, int B, int H, int S,
@@ -251,8 +253,7 @@ BW_API int bw_stream_status(void* stream);
  *   BW_OPT_PREFILL_KERNEL  0 (default): kernel 4 (the fastest at every
  *                          measured shape on B200);
  *                          1: two 128-row query blocks per CTA sharing each K/V
- *                          tile, one score buffer per block (also the fp32
- *                          MHA kernel);
+ *                          tile, one score buffer per block;
  *                          3: one query block per CTA, two score buffers, each
  *                          row's keys split over two threads with independent
  *                          softmax states merged by separate epilogue warps,

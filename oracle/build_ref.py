@@ -25,8 +25,16 @@ MHA_DATA_DIR) set to ``data`` relative to its working directory; main() runs
 B=16, H=12, S=1024, D=64, reports the precision of its output and of the
 files' "SDPA" output against the files' fp64 output, and times the kernel.
 
-The reference's tcgen05 kernels (src/SM103) cannot be built here: nvcc 12.9
-rejects their > 48 KB static shared memory.
+The reference's fused QK-norm + RoPE + attention program
+(src/SM103/attention/GQA_fused_sm103.cu) is WMMA code and compiles for sm_100a.
+Its ground truth for the fused op is two naive GPU kernels, ``ref_norm_rope``
+and ``ref_attention`` (:328-420); ``oracle/ref_fused_driver.cu`` includes that
+file unmodified (its main() renamed) and runs those two kernels on inputs given
+in files, into ``oracle/_ref/ref_fused`` (used by
+``tests/test_norm_rope_ref_gpu.py`` to pin the fused op).
+
+The reference's tcgen05 kernels (src/SM103, GQA_sm103*.cu) cannot be built
+here: nvcc 12.9 rejects their > 48 KB static shared memory.
 """
 from __future__ import annotations
 
@@ -38,6 +46,8 @@ HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "adhitya_gqa"
 OUT_MHA = HERE / "_ref" / "mha_sm120"
 OUT_GQA = HERE / "_ref" / "gqa_sm120"
+OUT_FUSED = HERE / "_ref" / "ref_fused"
+FUSED_DRIVER = HERE / "ref_fused_driver.cu"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
@@ -46,8 +56,8 @@ def default_reference_root() -> Path:
     return HERE.parent.parent / "reference"
 
 
-def _compile(src: Path, inc: Path, out: Path, extra: list[str], verbose: bool) -> Path:
-    if out.exists() and out.stat().st_mtime >= src.stat().st_mtime:
+def _compile(src: Path, inc: Path, out: Path, extra: list[str], verbose: bool, deps=()) -> Path:
+    if out.exists() and all(out.stat().st_mtime >= p.stat().st_mtime for p in (src, *deps)):
         return out
     out.parent.mkdir(exist_ok=True)
     cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", f"-I{inc}", *extra, str(src),
@@ -73,6 +83,9 @@ def build(reference_root: Path | None = None, verbose: bool = False) -> list[Pat
         built.append(_compile(att / "GQA_sm120.cu", inc, OUT_GQA, [], verbose))
     if (att / "MHA_sm120.cu").is_file():
         built.append(_compile(att / "MHA_sm120.cu", inc, OUT_MHA, ["-DMHA_DATA_DIR=data"], verbose))
+    fused = root / "src" / "SM103" / "attention" / "GQA_fused_sm103.cu"
+    if fused.is_file():
+        built.append(_compile(FUSED_DRIVER, inc, OUT_FUSED, [f"-I{fused.parent}"], verbose, deps=(fused,)))
     return built
 
 
