@@ -220,8 +220,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   if (cap > 0 && cap < ctas) ctas = (int)cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int poly = exp_poly_for(D);
-  cudaError_t e = kern == 5 ? bw::launch_fmha_fwd5(p, maps, poly, ctas, s)
-                  : kern == 4 ? bw::launch_fmha_fwd4(p, maps, poly, ctas, s)
+  cudaError_t e = kern == 4 ? bw::launch_fmha_fwd4(p, maps, poly, ctas, s)
                   : kern == 3 ? bw::launch_fmha_fwd3(p, maps, poly, ctas, s)
                             : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, poly, ctas, s);
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
@@ -682,7 +681,7 @@ int bw_set_option(int key, int64_t value) {
       g_max_ctas = value;
       return BW_OK;
     case BW_OPT_PREFILL_KERNEL:
-      if (value < 0 || value == 2 || value > 5) return BW_ERR_SHAPE;
+      if (value < 0 || value == 2 || value > 4) return BW_ERR_SHAPE;
       g_prefill_kernel = value;
       return BW_OK;
     case BW_OPT_EXP_POLY:

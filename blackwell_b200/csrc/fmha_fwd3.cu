@@ -74,8 +74,8 @@ constexpr int kMaxSlots = 12;
 template <int D, int V>
 struct Split {
   static constexpr int N = 2;                      // softmax warpgroups
-  static constexpr int NACC = V == 4 ? 1 : 2;      // O accumulators
-  static constexpr int NB = V == 5 ? 2 : ((V == 4 || D == 64) ? 3 : 2);
+  static constexpr int NACC = V == 3 ? 2 : 1;      // O accumulators
+  static constexpr int NB = (V == 4 || D == 64) ? 3 : 2;
   static constexpr int kKeys = 128 / N;            // keys per part (V = 3)
   static constexpr int kOCol = NB * 128;           // first TMEM column of O_0
   // softmax (4 N warps), output epilogue (4 warps), producer / PV issuer /
@@ -316,15 +316,7 @@ __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
         BW_TRACE_AT(true, 6, g);
         tc_fence_after();
         const uint32_t va = v_lo0 + (e % NS) * (uint32_t)(L::kTile / 16);
-        if constexpr (V == 5) {
-          // O_buf += P(g) V(g): the stream of the tile's parity has its own
-          // accumulator; the first tile of each stream in the segment (j < 2)
-          // starts it afresh
-#pragma unroll
-          for (int ks = 0; ks < kRows / 16; ++ks)
-            mma_ts_lh(tmem + Split<D, V>::kOCol + buf * D, tmem + buf * 128 + ks * 8, va + (ks * 16 * 128) / 16, HI,
-                      IDESC_PV, (ks > 0 || j >= 2) ? 1u : 0u);
-        } else if constexpr (V == 3) {
+        if constexpr (V == 3) {
           // part q: O_q += P_q (TMEM columns q K .. q K + K/2 - 1 of the buffer, K = keys
           // per part) * V rows q K .. q K + K - 1; k-step ks covers V rows 16 ks .. 16 ks + 15
           constexpr int KSP = Split<D, V>::kKeys / 16;   // k-steps per part
@@ -655,122 +647,6 @@ __device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
   }
 }
 
-// ------------------------------------------------- softmax warps, kernel 5
-// Two independent streams per query tile: warpgroup s (warps 4s .. 4s + 3)
-// takes the key tiles whose global index g has g % 2 == s, one query row per
-// thread (TMEM lane t % 128, all 128 keys of the tile), with its own running
-// max and sum and its own accumulator O_s (PV of its tiles only); the
-// epilogue merges the two streams per row.  The chain of a stream is
-// S(g) -> softmax -> P(g) -> PV(g) -> QK(g + 2) -> S(g + 2), while the other
-// stream's tile fills the tensor core, and the two warps of an SM
-// sub-partition work on different tiles, offset by about half a period, so
-// one's exponentials overlap the other's loads, max and stores.  O_s is
-// rescaled without waiting: its last PV (tile g - 2) completed before QK(g)
-// was issued into the same buffer.
-template <int D, int POLY>
-__device__ void softmax5(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
-  using L = L3<D>;
-  using Split = bw::Split<D, 5>;
-  constexpr int K = kRows;
-  const int rl = t & 127, st = t >> 7;
-  const uint32_t lane_off = (uint32_t)((rl >> 5) * 32) << 16;
-  const uint32_t s_tmem = tmem + lane_off + st * 128;
-  const uint32_t o_own = tmem + lane_off + Split::kOCol + st * D;
-  const float c = p.scale_log2;
-  float2* xch = reinterpret_cast<float2*>(smem + L::kX);
-  uint32_t tc = 0, itn = 0;
-
-  for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
-    const Item3 it = decode_item3(p, idx);
-    for (int sg = 0; sg < it.nseg; ++sg) {
-    const int n = sg == 0 ? it.n[0] : it.n[1];
-    const int qt = sg == 0 ? it.qt[0] : it.qt[1];
-    const int row = qt * kRows + rl;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool first = true;
-    for (int j = (int)((tc + st) & 1); j < n; j += 2) {
-      const uint32_t g = tc + j;          // g % 2 == st
-      if (!wc.wait(&bars.s_full[st], (g >> 1) & 1)) return;
-      tc_fence_after();
-      uint32_t r[K];
-      tmem_ld128(s_tmem, r);
-      float* s = reinterpret_cast<float*>(r);
-      const int kv0 = j * kRows;
-      if ((p.causal && kv0 + K - 1 > p.q_offset + qt * kRows) || kv0 + K > p.Skv) {
-        int lim = p.Skv - kv0;
-        if (p.causal) lim = min(lim, p.q_offset + row + 1 - kv0);
-#pragma unroll
-        for (int i = 0; i < K; ++i)
-          if (i >= lim) s[i] = -INFINITY;
-      }
-      float mx;
-      {
-        float a[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) a[u] = fmaxf(s[u], s[8 + u]);
-#pragma unroll
-        for (int i = 16; i < K; i += 16)
-#pragma unroll
-          for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
-        mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
-      }
-      const float m_cand = mx * c;
-      float corr = 1.f;
-      const bool upd = m_cand > m_run + 8.f;
-      if (upd) {
-        corr = ex2_mufu(m_run - m_cand);
-        m_run = m_cand;
-      }
-      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
-      const f2 cc2{c, c}, nm2{-msub, -msub};
-      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
-#pragma unroll
-      for (int k = 0; k < K / 2; ++k) {
-        const f2 x = ffma2(f2{s[2 * k], s[2 * k + 1]}, cc2, nm2);
-        f2 e;
-        if ((k & 7) < POLY) {
-          e = ex2_poly2(x);
-        } else {
-          e.x = ex2_mufu(x.x);
-          e.y = ex2_mufu(x.y);
-        }
-        if ((k & 3) == 0) acc0 = fadd2(acc0, e);
-        else if ((k & 3) == 1) acc1 = fadd2(acc1, e);
-        else if ((k & 3) == 2) acc2 = fadd2(acc2, e);
-        else acc3 = fadd2(acc3, e);
-        r[k] = pack_bf16_3(e.x, e.y);     // P (bf16): key k at column k / 2
-      }
-      acc0 = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
-      l_run = l_run * corr + (acc0.x + acc0.y);
-      tmem_st32(s_tmem, r);
-      tmem_st32(s_tmem + 32, r + 32);
-      if (!first && __any_sync(0xffffffffu, upd)) {
-#pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t o[32];
-          tmem_ld32(o_own + c0, o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-          tmem_st32(o_own + c0, o);
-        }
-      }
-      first = false;
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if ((t & 31) == 0) mbar_arrive(&bars.p_full[st]);
-    }
-    // hand the row's (m, l) of this stream to the epilogue warps
-    if (itn > 0 && !wc.wait(&bars.xch_empty, (itn - 1) & 1)) return;
-    xch[st * kRows + rl] = make_float2(m_run, l_run);
-    __syncwarp();
-    if ((t & 31) == 0) mbar_arrive(&bars.xch_full);
-    tc += n;
-    ++itn;
-    }
-  }
-}
-
 // ---------------------------------------------------------- epilogue warps
 // Thread t (0 .. 127): row t of every segment's query tile (TMEM lane t).  Per
 // segment: merge the parts of the row from their (m, l) (m = max_q m_q,
@@ -828,16 +704,12 @@ __device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sm
         uint32_t x[32];
         tmem_ld32(o0 + c0, x);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = lp[0] > 0.f ? __uint_as_float(x[i]) * w[0] : 0.f;
+        for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(x[i]) * w[0];
 #pragma unroll
         for (int q = 1; q < N; ++q) {
           tmem_ld32(o0 + q * D + c0, x);
-          // an accumulator that no tile of this segment reached holds stale
-          // columns: skipped, not multiplied by its zero weight
-          if (lp[q] > 0.f) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(x[i]), w[q], acc[i]);
-          }
+          for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(x[i]), w[q], acc[i]);
         }
         // columns c0 .. c0 + 31: panel c0 / 64, 16-byte chunks (c0 % 64) / 8 + i
 #pragma unroll
@@ -894,7 +766,7 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
     }
     for (int b = 0; b < Split::NB; ++b) {
       mbar_init(&bars.s_full[b], 1);
-      mbar_init(&bars.p_full[b], V == 5 ? 4 : 4 * Split::N);   // one arrival per softmax warp of the tile
+      mbar_init(&bars.p_full[b], 4 * Split::N);   // one arrival per softmax warp
     }
     for (int b = 0; b < Split::NB; ++b) mbar_init(&bars.pv_done[b], 1);
     mbar_init(&bars.qk_done, 1);
@@ -924,18 +796,14 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
   WaitCtl wc{&bars.abort_flag, p.err, p.timeout_ns, warp};
 
   // Register split (the block is launched with 128 per thread, 65536 in all):
-  // kernels 3 / 4: softmax 2 x 128 x 168 + epilogue 128 x 128 + producer /
-  // issuers 128 x 40 = 64512; kernel 5 (128 scores per softmax thread):
-  // 2 x 128 x 192 + 128 x 88 + 128 x 40 = 65536.
-  constexpr int kRegSoft = V == 5 ? 192 : 168, kRegEpi = V == 5 ? 88 : 128;
-  static_assert(256 * kRegSoft + 128 * kRegEpi + 128 * 40 <= 65536, "register split");
+  // softmax 2 x 128 x 168 + epilogue 128 x 128 + producer / issuers 128 x 40
+  // = 64512.
   if (warp < kSoftWarps) {
-    reg_alloc<kRegSoft>();
+    reg_alloc<168>();
     if constexpr (V == 3) softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
-    else if constexpr (V == 5) softmax5<D, POLY>(p, smem, bars, wc, tmem, tid);
     else softmax4<D, POLY>(p, smem, bars, wc, tmem, tid);
   } else if (warp < kEpilogue + 4) {
-    reg_dealloc<kRegEpi>();   // states this role's bound to the register allocator
+    reg_dealloc<128>();   // keeps the launch count; states this role's bound to the register allocator
     epilogue3<D, V>(p, maps, smem, bars, wc, tmem, tid - 32 * kEpilogue);
     // the warp's output stores read shared memory until they complete
     if (lane == 0) bulk_wait0();
@@ -990,13 +858,6 @@ cudaError_t launch_fmha_fwd4(const FmhaParams& p, const FmhaMaps& maps, int exp_
                              cudaStream_t stream) {
   if (p.D == 128) return launch3_poly<128, 4>(p, maps, exp_poly, num_sms, stream);
   if (p.D == 64) return launch3_poly<64, 4>(p, maps, exp_poly, num_sms, stream);
-  return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_fmha_fwd5(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
-                             cudaStream_t stream) {
-  if (p.D == 128) return launch3_poly<128, 5>(p, maps, exp_poly, num_sms, stream);
-  if (p.D == 64) return launch3_poly<64, 5>(p, maps, exp_poly, num_sms, stream);
   return cudaErrorInvalidValue;
 }
 

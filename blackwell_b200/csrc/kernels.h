@@ -74,11 +74,6 @@ cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_
 // the running max).
 cudaError_t launch_fmha_fwd4(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream);
-// Kernel 5: two independent softmax streams per query tile (even / odd key
-// tiles), one row per thread, two score buffers and two accumulators merged by
-// the epilogue.
-cudaError_t launch_fmha_fwd5(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
-                             cudaStream_t stream);
 
 // Split-KV single-token decode over ragged, contiguous per-sequence KV.
 struct DecodeParams {

@@ -4,13 +4,15 @@
 //
 //   bw_harness <mode> [--B n] [--Hq n] [--Hkv n] [--S n] [--Sq n] [--Skv n] [--D n]
 //              [--data DIR] [--iters n] [--warmup n] [--tol x]
-//   mode: gqa | gqa_causal | gqa_split | mha
+//   mode: gqa | gqa_causal | gqa_split | mha | mha_f32
 //
 // Files (headerless float32, the reference's format; base/baseline_gqa.py:165-170):
 //   gqa:        DIR/gqa_{q,k,v,o,lse}.bin           (src/SM120/attention/GQA_sm120.cu:427-433)
 //   gqa_causal: DIR/gqa_causal_{q,k,v,o,lse}.bin
 //   gqa_split:  DIR/gqa_split_{q,k,v,o,lse}.bin     (adhitya_GQA.cu:243-255)
 //   mha:        DIR/mha_{q,k,v,out}.bin             (MHA_sm120.cu:314-318; bf16 compute here)
+//   mha_f32:    the same files, fp32 in / out through launch_mha_f32 (the
+//               reference's mha_v3_tc call shape; 3xTF32, D = 64)
 // Inputs are narrowed to bf16 as the reference's loaders do.  Without the
 // files the inputs are N(0,1) from a fixed seed and only the benchmark runs.
 //
@@ -47,7 +49,7 @@ struct Args {
 
 int usage() {
   std::fprintf(stderr,
-               "usage: bw_harness gqa|gqa_causal|gqa_split|mha [--B n] [--Hq n] [--Hkv n] [--S n] [--Sq n] "
+               "usage: bw_harness gqa|gqa_causal|gqa_split|mha|mha_f32 [--B n] [--Hq n] [--Hkv n] [--S n] [--Sq n] "
                "[--Skv n] [--D 64|128] [--data DIR] [--iters n] [--warmup n] [--tol x]\n");
   return 2;
 }
@@ -225,13 +227,70 @@ int run(const Args& a) {
   return ok ? 0 : 1;
 }
 
+// fp32 MHA through the reference's mha_v3_tc call shape (launch_mha_f32).
+int run_mha_f32(const Args& a) {
+  constexpr int D = 64;
+  const size_t n = (size_t)a.B * a.Hq * a.S * D;
+  const std::string pre = a.data + "/mha_";
+  const bool has_ref = file_has(pre + "q.bin", n) && file_has(pre + "k.bin", n) && file_has(pre + "v.bin", n) &&
+                       file_has(pre + "out.bin", n);
+  std::vector<float> q(n), k(n), v(n), o_ref, o(n);
+  if (has_ref) {
+    bw_compat::loadBin((pre + "q.bin").c_str(), q.data(), n);
+    bw_compat::loadBin((pre + "k.bin").c_str(), k.data(), n);
+    bw_compat::loadBin((pre + "v.bin").c_str(), v.data(), n);
+    o_ref.resize(n);
+    bw_compat::loadBin((pre + "out.bin").c_str(), o_ref.data(), n);
+    std::printf("Loaded reference data from %s*.bin\n", pre.c_str());
+  } else {
+    randn(q, 1);
+    randn(k, 2);
+    randn(v, 3);
+    std::printf("No matching reference files under %s -- random inputs, benchmark only\n", a.data.c_str());
+  }
+  float *dq, *dk, *dv, *dout;
+  CK(cudaMalloc(&dq, n * 4));
+  CK(cudaMalloc(&dk, n * 4));
+  CK(cudaMalloc(&dv, n * 4));
+  CK(cudaMalloc(&dout, n * 4));
+  CK(cudaMemcpy(dq, q.data(), n * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(dk, k.data(), n * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(dv, v.data(), n * 4, cudaMemcpyHostToDevice));
+  const float scale = 1.f / std::sqrt((float)D);
+  auto launch = [&]() { return bw_compat::launch_mha_f32<16, 32, D>(dq, dk, dv, dout, scale, a.S, a.B, a.Hq); };
+  std::printf("mha_f32: B=%d H=%d S=%d D=%d (%s)\n", a.B, a.Hq, a.S, D, bw_version());
+  const int rc = launch();
+  if (rc != BW_OK) {
+    std::fprintf(stderr, "launch failed: %s\n", bw_strerror(rc));
+    return 2;
+  }
+  CK(cudaDeviceSynchronize());
+  if (bw_stream_status(nullptr) != BW_OK) {
+    std::fprintf(stderr, "device-side error reported by bw_stream_status\n");
+    return 2;
+  }
+  bool ok = true;
+  if (has_ref) {
+    CK(cudaMemcpy(o.data(), dout, n * 4, cudaMemcpyDeviceToHost));
+    std::printf("\nCorrectness (tolerance atol = rtol = %.0e):\n", a.tol);
+    ok = check("O", o_ref, o, a.tol);
+  }
+  bench("bw_attn mha_f32", [&]() { launch(); }, a.iters, a.warmup, 4.0 * a.B * a.Hq * (double)a.S * a.S * D);
+  cudaFree(dq);
+  cudaFree(dk);
+  cudaFree(dv);
+  cudaFree(dout);
+  return ok ? 0 : 1;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
   if (argc < 2) return usage();
   Args a;
   a.mode = argv[1];
-  if (a.mode != "gqa" && a.mode != "gqa_causal" && a.mode != "gqa_split" && a.mode != "mha") return usage();
+  if (a.mode != "gqa" && a.mode != "gqa_causal" && a.mode != "gqa_split" && a.mode != "mha" && a.mode != "mha_f32")
+    return usage();
   for (int i = 2; i < argc; ++i) {
     const std::string k = argv[i];
     if (i + 1 >= argc) return usage();
@@ -250,6 +309,7 @@ int main(int argc, char** argv) {
     else return usage();
   }
   if (a.B <= 0 || a.Hq <= 0 || a.Hkv <= 0 || a.S <= 0 || a.iters <= 0 || a.warmup < 0) return usage();
+  if (a.mode == "mha_f32") return run_mha_f32(a);   // D = 64, the reference's instantiation
   if (a.D == 64) return run<64>(a);
   if (a.D == 128) return run<128>(a);
   return usage();

@@ -13,6 +13,7 @@
 #include <cstdio>
 
 #include <cuda_bf16.h>
+#include <cuda_runtime.h>
 
 #include "bw_attn.h"
 
@@ -45,6 +46,34 @@ template <int Br, int Bc, int D>
 inline int launch_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, __nv_bfloat16* O,
                       float scale, int S, int B, int H) {
   return bw_mha_fwd(Q, K, V, O, nullptr, B, H, S, D, scale, nullptr, nullptr);
+}
+
+// src/SM120/attention/MHA_sm120.cu:64-71 (mha_v3_tc: fp32 Q, K, V, O, scale, S),
+// launch :333-345.  The reference's call has no workspace slot, so this
+// launcher keeps one (for the 3xTF32 hi / lo split) in a cudaMalloc'd buffer it
+// grows on demand and reuses; it is not thread-safe and is released at process
+// exit.  B and H are explicit because the reference derives them from its grid.
+template <int Br, int Bc, int D>
+inline int launch_mha_f32(const float* Q, const float* K, const float* V, float* O, float scale, int S, int B,
+                          int H) {
+  struct Workspace {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    ~Workspace() {
+      if (ptr) cudaFree(ptr);
+    }
+  };
+  static Workspace ws;
+  const size_t need = bw_mha_f32_workspace_size(B, H, S, D);
+  if (need == 0) return BW_ERR_SHAPE;
+  if (need > ws.bytes) {
+    if (ws.ptr) cudaFree(ws.ptr);
+    ws.ptr = nullptr;
+    ws.bytes = 0;
+    if (cudaMalloc(&ws.ptr, need) != cudaSuccess) return BW_ERR_CUDA;
+    ws.bytes = need;
+  }
+  return bw_mha_fwd_f32(Q, K, V, O, nullptr, B, H, S, D, scale, nullptr, ws.ptr, ws.bytes, nullptr);
 }
 
 // Reads `n` float32 values from a headerless file written by the reference's

@@ -59,3 +59,27 @@ def test_harness_on_reference_files(tmp_path, golden):
     bad.tofile(data / "gqa_causal_o.bin")
     r = subprocess.run(args, capture_output=True, text=True, timeout=300)
     assert r.returncode == 1 and "don't match at index 17" in r.stdout
+
+
+@pytest.mark.gpu
+def test_harness_mha_f32_on_reference_files(tmp_path, golden):
+    """fp32 MHA through bw_compat::launch_mha_f32 (the reference's mha_v3_tc call
+    shape) on the reference's own fp32 fixture: the harness's check passes at a
+    1e-5 tolerance (3xTF32 accuracy); a corrupted expected output fails."""
+    g = golden("mha_fp32_d64")
+    q, k, v = (np.asarray(g[n], np.float32) for n in ("q_f32", "k_f32", "v_f32"))
+    B, H, S, D = q.shape
+    data = tmp_path / "data"
+    data.mkdir()
+    for name, arr in (("q", q), ("k", k), ("v", v), ("out", g["o_fp64"])):
+        np.asarray(arr, np.float32).tofile(data / f"mha_{name}.bin")
+    args = [str(HARNESS), "mha_f32", "--B", str(B), "--Hq", str(H), "--S", str(S), "--D", "64", "--data", str(data),
+            "--iters", "5", "--warmup", "2", "--tol", "1e-5"]
+    r = subprocess.run(args, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.count("Values match!") == 1 and "Median Time" in r.stdout
+    bad = np.asarray(g["o_fp64"], np.float32).copy()
+    bad.flat[5] += 1e-3
+    bad.tofile(data / "mha_out.bin")
+    r = subprocess.run(args, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 1 and "don't match at index 5" in r.stdout
