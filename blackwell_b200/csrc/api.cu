@@ -42,7 +42,7 @@ std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
 std::atomic<int64_t> g_exp_poly{-1};        // -1: per head dimension (kExpPolyD64 / kExpPolyD128)
-std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 4)
+std::atomic<int64_t> g_prefill_kernel{0};   // 0: default (kernel 5 at D = 64, else 4)
 
 // Measured defaults of the exponential split (of every 8 pairs, how many run as
 // the FMA-pipe polynomial) per head dimension.
@@ -182,7 +182,8 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
 
   if (q_offset < 0 || (lse_sh != 0 && lse_sh < Sq)) return BW_ERR_SHAPE;
   int kern = (int)g_prefill_kernel.load();
-  if (kern == 0) kern = 4;
+  if (kern == 0) kern = D == 64 ? 5 : 4;
+  if (kern == 5 && D != 64) kern = 4;   // kernel 5 exists for D = 64 only
   const uint32_t kv_rows = 128u;
   bw::FmhaMaps maps;
   if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
@@ -220,7 +221,8 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   if (cap > 0 && cap < ctas) ctas = (int)cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int poly = exp_poly_for(D);
-  cudaError_t e = kern == 4 ? bw::launch_fmha_fwd4(p, maps, poly, ctas, s)
+  cudaError_t e = kern == 5   ? bw::launch_fmha_fwd5(p, maps, poly, ctas, s)
+                  : kern == 4 ? bw::launch_fmha_fwd4(p, maps, poly, ctas, s)
                   : kern == 3 ? bw::launch_fmha_fwd3(p, maps, poly, ctas, s)
                             : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, poly, ctas, s);
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
@@ -681,7 +683,7 @@ int bw_set_option(int key, int64_t value) {
       g_max_ctas = value;
       return BW_OK;
     case BW_OPT_PREFILL_KERNEL:
-      if (value < 0 || value == 2 || value > 4) return BW_ERR_SHAPE;
+      if (value < 0 || value == 2 || value > 5) return BW_ERR_SHAPE;
       g_prefill_kernel = value;
       return BW_OK;
     case BW_OPT_EXP_POLY:

@@ -74,18 +74,18 @@ constexpr int kMaxSlots = 12;
 template <int D, int V>
 struct Split {
   static constexpr int N = 2;                      // softmax warpgroups
-  static constexpr int NACC = V == 3 ? 2 : 1;      // O accumulators
-  static constexpr int NB = (V == 4 || D == 64) ? 3 : 2;
+  static constexpr int NACC = (V == 3 || V == 5) ? 2 : 1;   // O accumulators
+  static constexpr int NB = (V >= 4 || D == 64) ? 3 : 2;
   static constexpr int kKeys = 128 / N;            // keys per part (V = 3)
   static constexpr int kOCol = NB * 128;           // first TMEM column of O_0
   // softmax (4 N warps), output epilogue (4 warps), producer / PV issuer /
   // QK issuer (+ one idle warp): four warpgroups for the register split
   static constexpr int kThreads = 512;
   static_assert(N == 2, "warpgroup roles assume two softmax warpgroups");
-  static_assert(NB * 128 + NACC * D <= 512, "TMEM: score buffers and accumulators");
+  static_assert(kOCol + NACC * D <= 512, "TMEM: score buffers, P buffers and accumulators");
 };
 
-template <int D>
+template <int D, int V = 4>
 struct L3 {
   static constexpr int kTile = kRows * D * 2;   // one 128-row bf16 tile
   static constexpr int kSub = kRows * 128;      // one 128-byte swizzle panel
@@ -152,9 +152,9 @@ __device__ __forceinline__ Item3 decode_item3(const FmhaParams& p, int idx) {
 // ------------------------------------------------------------ producer warp
 // Loads, per item, the Q tile and then the K / V tiles in the order the MMA
 // thread consumes them: K0, K1, then V(j), K(j + 2) for j = 0 .. n - 1.
-template <int D>
+template <int D, int V>
 __device__ void producer3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc) {
-  using L = L3<D>;
+  using L = L3<D, V>;
   constexpr int NS = L::NS;
   uint32_t ld = 0, qn = 0;
   uint32_t armed = 0;
@@ -244,7 +244,7 @@ __device__ __forceinline__ uint32_t pos_v(int j, int n) {
 
 template <int D, int V>
 __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
-  using L = L3<D>;
+  using L = L3<D, V>;
   constexpr int NS = L::NS;
   constexpr int SUB = L::kSub;
   constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 128, false);
@@ -293,7 +293,7 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
 
 template <int D, int V>
 __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
-  using L = L3<D>;
+  using L = L3<D, V>;
   constexpr int NS = L::NS;
   constexpr int SUB = L::kSub;
   constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, true);
@@ -326,6 +326,13 @@ __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
             mma_ts_lh(tmem + Split<D, V>::kOCol + q * D, tmem + buf * 128 + q * Split<D, V>::kKeys + kin * 8,
                       va + (ks * 16 * 128) / 16, HI, IDESC_PV, (kin > 0 || j > 0) ? 1u : 0u);
           }
+        } else if constexpr (V == 5) {
+          // key tile j accumulates into O_{j % 2} (the part that owns it)
+          const uint32_t o_col = Split<D, V>::kOCol + (uint32_t)(j & 1) * D;
+#pragma unroll
+          for (int ks = 0; ks < kRows / 16; ++ks)
+            mma_ts_lh(tmem + o_col, tmem + buf * 128 + ks * 8, va + (ks * 16 * 128) / 16, HI, IDESC_PV,
+                      (ks > 0 || j >= 2) ? 1u : 0u);
         } else {
           // O += P (bf16, key k at column k / 2 of the buffer) * V; k-step ks: keys 16 ks ..
 #pragma unroll
@@ -358,7 +365,7 @@ __device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
 // t / 128, i.e. keys part K .. part K + K - 1 of every key tile (K = 128 / N).
 template <int D, int POLY>
 __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
-  using L = L3<D>;
+  using L = L3<D, 3>;
   using Split = bw::Split<D, 3>;
   constexpr int K = Split::kKeys;
   const int rl = t & 127, part = t >> 7;
@@ -490,7 +497,7 @@ __device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
 // MMA reads it (key k at column k / 2).
 template <int D, int POLY>
 __device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
-  using L = L3<D>;
+  using L = L3<D, 4>;
   using Split = bw::Split<D, 4>;
   constexpr uint32_t NB = Split::NB;
   const int w = t >> 5, ln = t & 31;
@@ -647,6 +654,146 @@ __device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
   }
 }
 
+// ------------------------------------------------- softmax warps, kernel 5
+// D = 64 only.  The two softmax warpgroups own alternate key tiles of a query
+// tile: part q = t / 128 takes key tiles j = q, q + 2, .. and accumulates them
+// into its own O_q; thread t holds row t % 128 and all 128 scores of its tile
+// (32x32b shape).  The two warps of one SM sub-partition therefore work on
+// neighbouring key tiles, not on the same one, so one warp's barrier waits and
+// TMEM round trips overlap the other's exponentials.  Each part keeps its own
+// running max and sum; the epilogue merges the two accumulators as in kernel
+// 3.  TMEM: S_0 | S_1 | S_2 | O_0 | O_1 (3 x 128 + 2 x 64 columns); P(g) goes
+// over the first 64 columns of its score buffer.  A rescale of O_q at tile j
+// waits for PV(j - 2), the part's previous tile.
+template <int D, int POLY>
+__device__ void softmax5(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
+  using L = L3<D, 5>;
+  using Split = bw::Split<D, 5>;
+  constexpr uint32_t NB = Split::NB;
+  const int rl = t & 127, part = t >> 7;
+  const uint32_t lane_off = (uint32_t)((rl >> 5) * 32) << 16;
+  const uint32_t o_own = tmem + lane_off + Split::kOCol + part * D;
+  const float c = p.scale_log2;
+  float2* xch = reinterpret_cast<float2*>(smem + L::kX);
+  uint32_t tc = 0, itn = 0;
+  // Score buffer g % 3 is reused by tile g + 3, and a parity wait for S(g) is
+  // only exact once S(g - 3) is known complete.  A part skips the other part's
+  // tiles (up to three in a row across segment boundaries), so it first waits,
+  // in order, for every score tile before its own: those complete in order
+  // before S(g) anyway, so this adds no latency.
+  uint32_t s_next = 0;
+
+  for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
+    const Item3 it = decode_item3(p, idx);
+    for (int sg = 0; sg < it.nseg; ++sg) {
+    const int n = sg == 0 ? it.n[0] : it.n[1];
+    const int qt = sg == 0 ? it.qt[0] : it.qt[1];
+    const int row = qt * kRows + rl;
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int j = part; j < n; j += 2) {
+      const uint32_t g = tc + j, buf = g % NB;
+      const uint32_t s_tmem = tmem + lane_off + buf * 128;
+      for (; s_next <= g; ++s_next)
+        if (!wc.wait(&bars.s_full[s_next % NB], (s_next / NB) & 1)) return;
+      BW_TRACE_AT(t == 0, 0, g);
+      BW_TRACE_AT(t == 128, 4, g);
+      tc_fence_after();
+      uint32_t r[128];
+      tmem_ld128(s_tmem, r);
+      BW_TRACE_AT(t == 0, 1, g);
+      BW_TRACE_AT(t == 128, 18, g);
+      float* s = reinterpret_cast<float*>(r);
+      const int kv0 = j * kRows;
+      if ((p.causal && kv0 + kRows - 1 > p.q_offset + qt * kRows) || kv0 + kRows > p.Skv) {
+        int lim = p.Skv - kv0;
+        if (p.causal) lim = min(lim, p.q_offset + row + 1 - kv0);
+#pragma unroll
+        for (int i = 0; i < kRows; ++i)
+          if (i >= lim) s[i] = -INFINITY;
+      }
+      float mx;
+      {
+        float a[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a[u] = fmaxf(s[u], s[8 + u]);
+#pragma unroll
+        for (int i = 16; i < kRows; i += 16)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
+        mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+      }
+      const float m_cand = mx * c;
+      float corr = 1.f;
+      const bool upd = m_cand > m_run + 8.f;
+      if (upd) {
+        corr = ex2_mufu(m_run - m_cand);
+        m_run = m_cand;
+      }
+      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
+      const f2 cc2{c, c}, nm2{-msub, -msub};
+      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
+      uint32_t pk[kRows / 2];
+#pragma unroll
+      for (int k = 0; k < kRows / 2; ++k) {
+        const f2 x = ffma2(f2{s[2 * k], s[2 * k + 1]}, cc2, nm2);
+        f2 e;
+        if ((k & 7) < POLY) {
+          e = ex2_poly2(x);
+        } else {
+          e.x = ex2_mufu(x.x);
+          e.y = ex2_mufu(x.y);
+        }
+        pk[k] = pack_bf16_3(e.x, e.y);
+        if ((k & 3) == 0) acc0 = fadd2(acc0, e);
+        else if ((k & 3) == 1) acc1 = fadd2(acc1, e);
+        else if ((k & 3) == 2) acc2 = fadd2(acc2, e);
+        else acc3 = fadd2(acc3, e);
+      }
+      acc0 = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
+      l_run = l_run * corr + (acc0.x + acc0.y);
+      BW_TRACE_AT(t == 0, 2, g);
+      BW_TRACE_AT(t == 128, 19, g);
+      // P (bf16, key k at column k / 2) over the first 64 columns of the buffer
+      tmem_st32(s_tmem, pk);
+      tmem_st32(s_tmem + 32, pk + 32);
+      if (j >= 2 && __any_sync(0xffffffffu, upd)) {
+        // O_part must hold PV(j - 2) before it is rescaled (exact parity: QK(g)
+        // waited for PV(g - 3), so PV(g - 5) is complete)
+        if (!wc.wait(&bars.pv_done[(g - 2) % NB], ((g - 2) / NB) & 1)) return;
+        tc_fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(o_own + c0, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+          tmem_st32(o_own + c0, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if ((t & 31) == 0) mbar_arrive(&bars.p_full[buf]);
+      BW_TRACE_AT(t == 0, 3, g);
+      BW_TRACE_AT(t == 128, 5, g);
+      BW_TRACE_AT((t & 31) == 0 && t < 256, 10 + (t >> 5), g);
+    }
+    // (m, l) of the row's part for the epilogue (a part with no key tile in
+    // this segment hands over m = -inf, l = 0)
+    if (itn > 0 && !wc.wait(&bars.xch_empty, (itn - 1) & 1)) return;
+    xch[part * kRows + rl] = make_float2(m_run, l_run);
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&bars.xch_full);
+    tc += n;
+    ++itn;
+    }
+  }
+}
+
+// 16 or 32 consecutive TMEM columns of this thread's lane (32x32b shape).
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
+
 // ---------------------------------------------------------- epilogue warps
 // Thread t (0 .. 127): row t of every segment's query tile (TMEM lane t).  Per
 // segment: merge the parts of the row from their (m, l) (m = max_q m_q,
@@ -660,7 +807,7 @@ __device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
 template <int D, int V>
 __device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc,
                           uint32_t tmem, int t) {
-  using L = L3<D>;
+  using L = L3<D, V>;
   constexpr int N = Split<D, V>::NACC;
   const int ln = t & 31, wq = t >> 5;
   const uint32_t o0 = tmem + ((uint32_t)(wq * 32) << 16) + Split<D, V>::kOCol;
@@ -698,22 +845,27 @@ __device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sm
       __syncwarp();
       if (!wc.wait(&bars.o_full, itn & 1)) return;
       tc_fence_after();
+      // columns per TMEM load: 16 for kernel 5, whose epilogue runs in 80 registers
+      constexpr int CW = V == 5 ? 16 : 32;
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        float acc[32];
-        uint32_t x[32];
-        tmem_ld32(o0 + c0, x);
+      for (int c0 = 0; c0 < D; c0 += CW) {
+        float acc[CW];
+        uint32_t x[CW];
+        tmem_ld_cols(o0 + c0, x);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(x[i]) * w[0];
+        for (int i = 0; i < CW; ++i) acc[i] = __uint_as_float(x[i]) * w[0];
 #pragma unroll
         for (int q = 1; q < N; ++q) {
-          tmem_ld32(o0 + q * D + c0, x);
+          tmem_ld_cols(o0 + q * D + c0, x);
+          // kernel 5: a part that owned no key tile of the segment (n = 1) never
+          // wrote its accumulator, whose stale contents must not reach O
+          if (V == 5 && w[q] == 0.f) continue;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(x[i]), w[q], acc[i]);
+          for (int i = 0; i < CW; ++i) acc[i] = fmaf(__uint_as_float(x[i]), w[q], acc[i]);
         }
-        // columns c0 .. c0 + 31: panel c0 / 64, 16-byte chunks (c0 % 64) / 8 + i
+        // columns c0 .. c0 + CW - 1: panel c0 / 64, 16-byte chunks (c0 % 64) / 8 + i
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < CW / 8; ++i) {
           const int ch = (c0 & 63) / 8 + i;
           *reinterpret_cast<uint4*>(stg + (c0 / 64) * (32 * 128) + ln * 128 + ((ch ^ (ln & 7)) << 4)) =
               make_uint4(pack_bf16_3(acc[8 * i], acc[8 * i + 1]), pack_bf16_3(acc[8 * i + 2], acc[8 * i + 3]),
@@ -742,7 +894,7 @@ template <int D, int POLY, int V>
 __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
   using Split = bw::Split<D, V>;
   static_assert(Split::kThreads == 512, "launch bounds");
-  using L = L3<D>;
+  using L = L3<D, V>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   if (pad > (uint32_t)kAlignSlack) {
@@ -766,7 +918,7 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
     }
     for (int b = 0; b < Split::NB; ++b) {
       mbar_init(&bars.s_full[b], 1);
-      mbar_init(&bars.p_full[b], 4 * Split::N);   // one arrival per softmax warp
+      mbar_init(&bars.p_full[b], V == 5 ? 4 : 4 * Split::N);   // one arrival per softmax warp of the tile
     }
     for (int b = 0; b < Split::NB; ++b) mbar_init(&bars.pv_done[b], 1);
     mbar_init(&bars.qk_done, 1);
@@ -797,20 +949,24 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
 
   // Register split (the block is launched with 128 per thread, 65536 in all):
   // softmax 2 x 128 x 168 + epilogue 128 x 128 + producer / issuers 128 x 40
-  // = 64512.
+  // = 64512; kernel 5 (a whole 128-score row per thread): softmax 2 x 128 x
+  // 200 + epilogue 128 x 80 + producer / issuers 128 x 32 = 65536.
+  constexpr int kSoftRegs = V == 5 ? 200 : 168, kEpiRegs = V == 5 ? 80 : 128, kAuxRegs = V == 5 ? 32 : 40;
+  static_assert(2 * 128 * kSoftRegs + 128 * kEpiRegs + 128 * kAuxRegs <= 65536, "register split");
   if (warp < kSoftWarps) {
-    reg_alloc<168>();
+    reg_alloc<kSoftRegs>();
     if constexpr (V == 3) softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
+    else if constexpr (V == 5) softmax5<D, POLY>(p, smem, bars, wc, tmem, tid);
     else softmax4<D, POLY>(p, smem, bars, wc, tmem, tid);
   } else if (warp < kEpilogue + 4) {
-    reg_dealloc<128>();   // keeps the launch count; states this role's bound to the register allocator
+    reg_dealloc<kEpiRegs>();   // 128 keeps the launch count; states this role's bound to the register allocator
     epilogue3<D, V>(p, maps, smem, bars, wc, tmem, tid - 32 * kEpilogue);
     // the warp's output stores read shared memory until they complete
     if (lane == 0) bulk_wait0();
   } else {
-    reg_dealloc<40>();
+    reg_dealloc<kAuxRegs>();
     if (lane == 0) {
-      if (warp == kProducer) producer3<D>(p, maps, smem, bars, wc);
+      if (warp == kProducer) producer3<D, V>(p, maps, smem, bars, wc);
       else if (warp == kPvIssuer) pv_issuer3<D, V>(p, smem, bars, wc, tmem);
       else if (warp == kQkIssuer) qk_issuer3<D, V>(p, smem, bars, wc, tmem);
     }
@@ -825,7 +981,7 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
 
 template <int D, int POLY, int V>
 cudaError_t launch3(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
-  constexpr int bytes = L3<D>::kBytes + kAlignSlack;
+  constexpr int bytes = L3<D, V>::kBytes + kAlignSlack;
   auto kern = fmha_fwd3_kernel<D, POLY, V>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
@@ -851,6 +1007,12 @@ cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_
                              cudaStream_t stream) {
   if (p.D == 128) return launch3_poly<128, 3>(p, maps, exp_poly, num_sms, stream);
   if (p.D == 64) return launch3_poly<64, 3>(p, maps, exp_poly, num_sms, stream);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_fmha_fwd5(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
+                             cudaStream_t stream) {
+  if (p.D == 64) return launch3_poly<64, 5>(p, maps, exp_poly, num_sms, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -74,6 +74,10 @@ cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_
 // the running max).
 cudaError_t launch_fmha_fwd4(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream);
+// Kernel 5 (D = 64): three score buffers, two O accumulators; the two softmax
+// warpgroups own alternate key tiles, one row per thread.
+cudaError_t launch_fmha_fwd5(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
+                             cudaStream_t stream);
 
 // Split-KV single-token decode over ragged, contiguous per-sequence KV.
 struct DecodeParams {

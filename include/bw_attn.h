@@ -250,8 +250,9 @@ BW_API int bw_stream_status(void* stream);
  *                          are computed by an FMA-pipe polynomial instead of
  *                          MUFU ex2: 0, 2, 3 or 4; -1 (default) picks the
  *                          measured best per head dimension
- *   BW_OPT_PREFILL_KERNEL  0 (default): kernel 4 (the fastest at every
- *                          measured shape on B200);
+ *   BW_OPT_PREFILL_KERNEL  0 (default): kernel 5 at D = 64, kernel 4 at
+ *                          D = 128 (the fastest at every measured shape on
+ *                          B200);
  *                          1: two 128-row query blocks per CTA sharing each K/V
  *                          tile, one score buffer per block;
  *                          3: one query block per CTA, two score buffers, each
@@ -260,7 +261,11 @@ BW_API int bw_stream_status(void* stream);
  *                          separate QK^T and PV issuing threads;
  *                          4: as 3 with three score buffers and one O
  *                          accumulator (four threads per row share the
- *                          running max), so QK^T never waits for PV.
+ *                          running max), so QK^T never waits for PV;
+ *                          5 (D = 64; at D = 128 it selects 4): three score
+ *                          buffers and two O accumulators, the two softmax
+ *                          warpgroups taking alternate key tiles (one row per
+ *                          thread), merged by the epilogue warps.
  *                          BW_OPT_P_IN_TMEM applies to kernel 1 only. */
 enum {
   BW_OPT_TIMEOUT_NS = 1,

@@ -139,8 +139,8 @@ def test_prefill_kernel_option_values():
     lib = _ffi.lib()
     old = lib.bw_get_option(_ffi.BW_OPT_PREFILL_KERNEL)
     assert old == 0                                   # default kernel
-    for v in (0, 1, 3, 4):
+    for v in (0, 1, 3, 4, 5):
         assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == 0
-    for v in (-1, 2, 5):
+    for v in (-1, 2, 6):
         assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == _ffi.BW_ERR_SHAPE
     lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, old)

@@ -16,11 +16,13 @@ pytestmark = pytest.mark.gpu
 GOLDEN_GQA = ["gqa_nc_d128", "gqa_causal_d128", "gqa_causal_d64_g3_rand", "gqa_causal_d64_ragged", "gqa_split_d64"]
 
 
-@pytest.fixture(scope="module", params=[(4, 1), (3, 1), (1, 1), (1, 0)],
-                ids=["k4_one_acc", "k3_split_rows", "k1_p_tmem", "k1_p_smem"])
+@pytest.fixture(scope="module", params=[(5, 1), (4, 1), (3, 1), (1, 1), (1, 0)],
+                ids=["k5_alt_tiles", "k4_one_acc", "k3_split_rows", "k1_p_tmem", "k1_p_smem"])
 def p_variant(request):
-    """Kernel variants: one query block with three score buffers and one
-    accumulator, four threads per row (kernel 4); one query block with two
+    """Kernel variants: alternate key tiles per softmax warpgroup into two
+    accumulators (kernel 5, D = 64; kernel 4 at D = 128); one query block with
+    three score buffers and one accumulator, four threads per row (kernel 4);
+    one query block with two
     score buffers and rows split over two threads (kernel 3), or two query blocks with P fed to the PV MMA from TMEM or
     shared memory (kernel 1)."""
     import blackwell_b200 as bw
@@ -71,6 +73,8 @@ CASES = [
     (1, 6, 2, 257, 640, 64, False),    # split lengths
     (1, 4, 2, 640, 200, 128, True),    # Sq > Skv, causal
     (1, 2, 1, 1, 1000, 128, False),    # one query row
+    (2, 6, 2, 640, 640, 64, True),     # odd key-tile counts per causal segment (5 + 1, 3 + 3)
+    (1, 4, 1, 1000, 1000, 64, True),   # 8 query tiles: segments of 8 + 1 .. 5 + 4 key tiles
 ]
 
 
@@ -283,15 +287,15 @@ def test_mha_fp32_strided_out_and_reuse():
         assert np.abs(out.transpose(1, 2).cpu().numpy() - ro).max() <= 1e-5
 
 
-@pytest.mark.parametrize("kernel", [4, 3, 1])
+@pytest.mark.parametrize("kernel,D", [(4, 128), (3, 128), (1, 128), (5, 64), (4, 64)])
 @pytest.mark.parametrize("q_scale,causal", [(12.0, True), (12.0, False), (0.02, True)])
-def test_logit_range_stress(kernel, q_scale, causal):
+def test_logit_range_stress(kernel, D, q_scale, causal):
     """Large logits (q scaled up: the running max moves by far more than the
-    lazy-rescale threshold, and the two halves of a row in kernel 3 end with
-    very different maxima) and nearly flat ones, against fp64 rows."""
+    lazy-rescale threshold, and the two halves of a row in kernels 3 and 5 end
+    with very different maxima) and nearly flat ones, against fp64 rows."""
     import blackwell_b200 as bw
     from blackwell_b200 import _ffi
-    B, Hq, Hkv, S, D = 1, 4, 2, 640, 128
+    B, Hq, Hkv, S = 1, 4, 2, 640
     g = torch.Generator().manual_seed(int(q_scale * 10) + causal)
     # keys with a growing trend so that later tiles keep raising the row max
     q = (torch.randn(B, Hq, S, D, generator=g) * q_scale / math.sqrt(D)).bfloat16()
