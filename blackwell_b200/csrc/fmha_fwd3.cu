@@ -845,7 +845,7 @@ __device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sm
       __syncwarp();
       if (!wc.wait(&bars.o_full, itn & 1)) return;
       tc_fence_after();
-      // columns per TMEM load: 16 for kernel 5, whose epilogue runs in 80 registers
+      // columns per TMEM load: 16 for kernel 5, whose epilogue runs in 64 registers
       constexpr int CW = V == 5 ? 16 : 32;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += CW) {
@@ -950,8 +950,9 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
   // Register split (the block is launched with 128 per thread, 65536 in all):
   // softmax 2 x 128 x 168 + epilogue 128 x 128 + producer / issuers 128 x 40
   // = 64512; kernel 5 (a whole 128-score row per thread): softmax 2 x 128 x
-  // 200 + epilogue 128 x 80 + producer / issuers 128 x 32 = 65536.
-  constexpr int kSoftRegs = V == 5 ? 200 : 168, kEpiRegs = V == 5 ? 80 : 128, kAuxRegs = V == 5 ? 32 : 40;
+  // 200 + epilogue 128 x 64 + producer / issuers 128 x 48 = 65536 (no spills;
+  // issuers at 32 spilled, run once per key tile).
+  constexpr int kSoftRegs = V == 5 ? 200 : 168, kEpiRegs = V == 5 ? 64 : 128, kAuxRegs = V == 5 ? 48 : 40;
   static_assert(2 * 128 * kSoftRegs + 128 * kEpiRegs + 128 * kAuxRegs <= 65536, "register split");
   if (warp < kSoftWarps) {
     reg_alloc<kSoftRegs>();
