@@ -10,7 +10,8 @@
 // Causal calls are cut along the sequence: query rows [s0, s1) need keys
 // [0, s1) only, all of which have arrived with chunks 0 .. c, so chunk c runs
 // as a split-length call with a query offset of s0 (rows in multiples of 128).
-// Non-causal calls are cut along the batch.  The copies are strided 2-D
+// Non-causal calls are cut along the batch.  Chunks shrink from first to last
+// (weights nc .. 1), so that little work remains once the last copy-in lands.  The copies are strided 2-D
 // copies (one per tensor and chunk), so both host layouts work without a
 // staging copy.  Overlap needs page-locked host memory.
 #include <mutex>
@@ -125,12 +126,16 @@ int bw_attn_fwd_host(const void* Q, const void* K, const void* V, void* O, float
   int nc = chunks <= 0 ? 4 : chunks;
   nc = nc > kMaxChunks ? kMaxChunks : nc;
   nc = nc > (by_rows ? ntiles : B) ? (by_rows ? ntiles : B) : nc;
+  // Chunk sizes fall linearly (weights nc, nc - 1, .., 1): what is left after
+  // the last copy-in (the last chunk's kernel and copy-out) is small, while the
+  // copy-in stream, the bound, runs without gaps from the first chunk on.
+  const int units = by_rows ? ntiles : B;
+  const int64_t wsum = (int64_t)nc * (nc + 1) / 2;
   auto bound = [&](int c) -> int {
-    if (by_rows) {
-      const int r = (int)(((int64_t)c * ntiles + nc / 2) / nc) * 128;
-      return c == nc ? S : (r > S ? S : r);
-    }
-    return (int)(((int64_t)c * B + nc / 2) / nc);
+    const int64_t w = (int64_t)c * nc - (int64_t)c * (c - 1) / 2;   // weights of chunks 0 .. c - 1
+    const int u = (int)((w * units + wsum / 2) / wsum);
+    if (by_rows) return c == nc ? S : (u * 128 > S ? S : u * 128);
+    return u;
   };
 
   cudaStream_t s_cmp = static_cast<cudaStream_t>(stream);

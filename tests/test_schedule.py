@@ -50,11 +50,23 @@ def test_causal_pairs_balance(nqt, q_offset):
 @pytest.mark.parametrize("S,chunks", [(4096, 8), (320, 3), (1000, 8), (64, 4), (777, 32), (128, 1)])
 def test_host_pipeline_sequence_chunks(S, chunks):
     """bw_attn_fwd_host cuts causal calls into <= chunks pieces whose bounds are
-    multiples of 128 rows (the query offset of each piece) and end at S."""
+    multiples of 128 rows (the query offset of each piece) and end at S; the
+    pieces shrink from first to last (weights nc .. 1), so the work left after
+    the last copy-in is the smallest piece."""
     ntiles = (S + 127) // 128
     nc = min(chunks, 32, ntiles)
-    bound = lambda c: S if c == nc else min(((c * ntiles + nc // 2) // nc) * 128, S)
+    wsum = nc * (nc + 1) // 2
+
+    def bound(c):
+        w = c * nc - c * (c - 1) // 2
+        u = (w * ntiles + wsum // 2) // wsum
+        return S if c == nc else min(u * 128, S)
+
     bounds = [bound(c) for c in range(nc + 1)]
     assert bounds[0] == 0 and bounds[-1] == S
-    assert all(b % 128 == 0 for b in bounds[:-1])
-    assert all(x < y for x, y in zip(bounds, bounds[1:]))
+    assert all(b % 128 == 0 for b in bounds if b < S)
+    assert all(x <= y for x, y in zip(bounds, bounds[1:]))
+    sizes = [y - x for x, y in zip(bounds, bounds[1:]) if y > x]
+    assert sizes[-1] == min(sizes)
+    if (S, chunks) == (4096, 8):
+        assert [z // 128 for z in sizes] == [7, 6, 6, 4, 4, 2, 2, 1]
