@@ -38,7 +38,6 @@ DeviceState g_dev[kMaxDevices];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 std::atomic<int64_t> g_timeout_ns{2000000000LL};
-std::atomic<int64_t> g_p_in_tmem{1};
 std::atomic<int64_t> g_debug_flags{0};
 std::atomic<int64_t> g_max_ctas{0};
 std::atomic<int64_t> g_exp_poly{-1};        // -1: per head dimension (kExpPolyD64 / kExpPolyD128)
@@ -189,7 +188,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   if (make_map_bhsd(&maps.q, Q, B, Hq, Sq, D, st.q) != BW_OK) return BW_ERR_CUDA;
   if (make_map_bhsd(&maps.k, K, B, Hkv, Skv, D, st.k, kv_rows) != BW_OK) return BW_ERR_CUDA;
   if (make_map_bhsd(&maps.v, V, B, Hkv, Skv, D, st.v, kv_rows) != BW_OK) return BW_ERR_CUDA;
-  if (kern >= 3 && make_map_out(&maps.o, O, B, Hq, Sq, D, st.o) != BW_OK) return BW_ERR_CUDA;
+  if (make_map_out(&maps.o, O, B, Hq, Sq, D, st.o) != BW_OK) return BW_ERR_CUDA;
 
   bw::FmhaParams p{};
   p.O = O;
@@ -208,9 +207,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_qtiles = (Sq + 127) / 128;
   p.n_kvtiles = (Skv + 127) / 128;
-  p.pair_heads = (G % 2 == 0) ? 1 : 0;
-  p.num_items = p.pair_heads ? B * (Hq / 2) * p.n_qtiles : B * Hq * ((p.n_qtiles + 1) / 2);
-  if (kern >= 3) p.num_items = B * Hq * (causal ? (p.n_qtiles + 1) / 2 : p.n_qtiles);
+  p.num_items = B * Hq * (causal ? (p.n_qtiles + 1) / 2 : p.n_qtiles);
   p.err = err_slot(dev, stream);
   p.timeout_ns = (uint64_t)g_timeout_ns.load();
   p.debug_flags = (int)g_debug_flags.load();
@@ -221,10 +218,7 @@ int attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE, i
   if (cap > 0 && cap < ctas) ctas = (int)cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int poly = exp_poly_for(D);
-  cudaError_t e = kern == 5   ? bw::launch_fmha_fwd5(p, maps, poly, ctas, s)
-                  : kern == 4 ? bw::launch_fmha_fwd4(p, maps, poly, ctas, s)
-                  : kern == 3 ? bw::launch_fmha_fwd3(p, maps, poly, ctas, s)
-                            : bw::launch_fmha_fwd(p, maps, g_p_in_tmem.load() != 0, poly, ctas, s);
+  cudaError_t e = kern == 5 ? bw::launch_fmha_fwd5(p, maps, poly, ctas, s) : bw::launch_fmha_fwd4(p, maps, poly, ctas, s);
   return e == cudaSuccess ? BW_OK : BW_ERR_CUDA;
 }
 
@@ -676,14 +670,13 @@ int bw_set_option(int key, int64_t value) {
       if (value <= 0) return BW_ERR_SHAPE;
       g_timeout_ns = value;
       return BW_OK;
-    case BW_OPT_P_IN_TMEM: g_p_in_tmem = value ? 1 : 0; return BW_OK;
     case BW_OPT_DEBUG_FLAGS: g_debug_flags = value; return BW_OK;
     case BW_OPT_MAX_CTAS:
       if (value < 0) return BW_ERR_SHAPE;
       g_max_ctas = value;
       return BW_OK;
     case BW_OPT_PREFILL_KERNEL:
-      if (value < 0 || value == 2 || value > 5) return BW_ERR_SHAPE;
+      if (value != 0 && value != 4 && value != 5) return BW_ERR_SHAPE;
       g_prefill_kernel = value;
       return BW_OK;
     case BW_OPT_EXP_POLY:
@@ -697,7 +690,6 @@ int bw_set_option(int key, int64_t value) {
 int64_t bw_get_option(int key) {
   switch (key) {
     case BW_OPT_TIMEOUT_NS: return g_timeout_ns.load();
-    case BW_OPT_P_IN_TMEM: return g_p_in_tmem.load();
     case BW_OPT_DEBUG_FLAGS: return g_debug_flags.load();
     case BW_OPT_MAX_CTAS: return g_max_ctas.load();
     case BW_OPT_EXP_POLY: return g_exp_poly.load();

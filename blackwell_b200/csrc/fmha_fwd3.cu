@@ -1,47 +1,37 @@
 // GQA / MHA flash-attention forward for sm_100a, one query tile per work item:
-// kernel 3 (double-buffered scores, each row split over two threads with
-// separate accumulators) and kernel 4 (three score buffers, one accumulator;
-// see Split below), the same roles and pipeline otherwise.
+// kernel 4 (three score buffers, one O accumulator; the default at D = 128) and
+// kernel 5 (D = 64: three score buffers, two O accumulators owned by the two
+// softmax warpgroups in turn), the same roles and pipeline otherwise.
 //
-// Same operator as fmha_fwd.cu (per query row i of head hq, KV head hq / G:
-// O[i] = softmax(scale * Q[i] K^T) V, LSE[i] = ln sum_j exp(scale * Q[i].K[j]),
-// optional causal mask j <= i), the behaviour of the reference's
+// Operator (per query row i of head hq, KV head hq / G):
+//   O[i] = softmax(scale * Q[i] K^T) V,  LSE[i] = ln sum_j exp(scale * Q[i].K[j]),
+// optional causal mask j <= q_offset + i; the behaviour of the reference's
 // launch_gqa_vN / gqa_causal launchers (src/SM103/attention/GQA_sm103.cu:5733-6516,
 // GQA_sm103_causal_v3.cu:2156-2180) and the split-length launcher
 // (src/SM120/attention/adhitya_GQA.cu:199-213).
 //
-// Design (one persistent CTA per SM, four warpgroups, N = 2):
-//   warps 0 .. 4N-1  softmax: one 128-row query tile; row r is shared by
-//                    thread r of warps 4q .. 4q+3 for q = 0 .. N-1 ("part" q
-//                    takes keys qK .. qK+K-1 of every key tile, K = 128 / N)
-//   warps 8 .. 11    epilogue: row r of each finished tile (merge, O, LSE)
+// Design (one persistent CTA per SM, four warpgroups):
+//   warps 0 .. 7     softmax: one 128-row query tile (two warpgroups)
+//   warps 8 .. 11    epilogue: row r of each finished tile (O / L, LSE; kernel
+//                    5 first merges its two accumulators)
 //   warp 12          TMA producer: the Q tile, then K and V tiles in MMA order
 //   warp 13          PV MMA issuer (one thread) and TMEM owner
 //   warp 14          QK^T MMA issuer (one thread); warp 15 idle
-// The parts of a row run independent online softmaxes (own running max and
-// sum) into their own accumulators O_q = sum over part-q keys of p V, and are
-// merged once per row by the epilogue warps:
-//   m = max_q m_q, w_q = 2^(m_q - m), L = sum_q l_q w_q,
-//   O = sum_q O_q w_q / L,  LSE = ln 2 (m + log2 L),
-// so the softmax warps go from a tile's last key tile straight to the next
-// tile's first (the merge, the O read and its store cost ~1.5k cycles per
-// tile, which on the softmax warps stalled the whole pipeline).
-// Tensor memory: S_0 .. S_{NB-1} (128 fp32 columns each; NB = 2 at D = 128,
-// 3 at D = 64) | O_0 .. O_{N-1} (D columns each).  Global key tile g (counted
-// over all items of the CTA) uses score buffer g % NB; part q writes its P
-// (bf16) over columns [qK, qK + K/2) of that buffer.  MMA order per item of n
-// key tiles:
-//   QK(0), QK(1), then for each j: PV(j), QK(j + 2)   (two issuing threads below)
+// Tensor memory: S_0 | S_1 | S_2 (128 fp32 columns each) | O (D columns;
+// kernel 5: O_0 | O_1).  Global key tile g (counted over all items of the
+// CTA) uses score buffer g % 3; the softmax writes its P (bf16) over the first
+// 64 columns of that buffer, and the PV MMA reads it from there (TS form).
+// MMA order per item of n key tiles:
+//   QK(0), QK(1), then for each j: PV(j), QK(j + 2)   (two issuing threads)
 // so while the softmax works on tile j the tensor core runs PV(j - 1) and
 // QK(j + 1) is already waiting in another buffer: the softmax of one tile
-// overlaps the MMAs of its neighbours instead of waiting for them, and the N
-// threads per row give each SM sub-partition N softmax warps to interleave.
-// (The two-query-block design of fmha_fwd.cu cannot double-buffer: two blocks
-// x (2 score buffers + O) needs 768 columns of the 512.)
+// overlaps the MMAs of its neighbours instead of waiting for them.  The
+// epilogue warpgroup takes the end of a tile (O read, division, store) off the
+// softmax warps, which go from a tile's last key tile straight to the next
+// tile's first.
 //
 // Online softmax in the log2 domain with the FlashAttention-4 lazy rescale
-// (running max raised only when a tile's max exceeds it by more than 8), as
-// in fmha_fwd.cu, per part.  A rescale of O_q at tile j first waits for PV(j - 1).
+// (running max raised only when a tile's max exceeds it by more than 8).
 #include "kernels.h"
 #include "ptx.cuh"
 #include "softmax_math.cuh"
@@ -57,26 +47,20 @@ constexpr int kAlignSlack = 512;
 constexpr int kSmemBudget = 232448 - kAlignSlack;
 constexpr int kMaxSlots = 12;
 
-// N threads per query row, each taking kKeys = 128 / N keys of every key tile
-// into its own accumulator O_part (D columns), and NB score buffers of 128
-// columns: TMEM holds S_0 .. S_{NB-1} | O_0 .. O_{N-1}, NB 128 + N D <= 512.
-// D = 128: N = 2, NB = 2.  D = 64: N = 2, NB = 3 (the third buffer lets
-// QK(g + 1) start before PV(g - 1) has finished; N = 4 with two buffers
-// measured slower, the PV -> QK chain bounding it).
-//
-// Variant V = 4 (kernel 4) keeps one accumulator O and three score buffers
-// (TMEM S_0 | S_1 | S_2 | O, 3 x 128 + D <= 512 columns), so that QK(g + 1)
-// never waits for PV(g - 1): each softmax warp covers 16 rows of its TMEM
-// lane quadrant through the 16-lane access shapes, four threads per row and
-// two rows per thread, and the four threads of a row share one running max
-// (two shuffles per row and tile), so all keys of a row accumulate into the
-// same O.
+// Kernel 4 (V = 4): one accumulator O and three score buffers (TMEM S_0 | S_1
+// | S_2 | O, 3 x 128 + D <= 512 columns), so that QK(g + 1) never waits for
+// PV(g - 1): each softmax warp covers 16 rows of its TMEM lane quadrant
+// through the 16-lane access shapes, four threads per row and two rows per
+// thread, and the four threads of a row share one running max (two shuffles
+// per row and tile), so all keys of a row accumulate into the same O.
+// Kernel 5 (V = 5, D = 64): the same three buffers and two accumulators
+// O_0 | O_1 (3 x 128 + 2 x 64 = 512 columns); see softmax5.
 template <int D, int V>
 struct Split {
+  static_assert(V == 4 || (V == 5 && D == 64), "kernel 4 (D = 64, 128) or kernel 5 (D = 64)");
   static constexpr int N = 2;                      // softmax warpgroups
-  static constexpr int NACC = (V == 3 || V == 5) ? 2 : 1;   // O accumulators
-  static constexpr int NB = (V >= 4 || D == 64) ? 3 : 2;
-  static constexpr int kKeys = 128 / N;            // keys per part (V = 3)
+  static constexpr int NACC = V == 5 ? 2 : 1;      // O accumulators
+  static constexpr int NB = 3;                     // score buffers
   static constexpr int kOCol = NB * 128;           // first TMEM column of O_0
   // softmax (4 N warps), output epilogue (4 warps), producer / PV issuer /
   // QK issuer (+ one idle warp): four warpgroups for the register split
@@ -223,8 +207,8 @@ __device__ void producer3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* sm
 // overlap the other's issue (an issuing thread blocks while the tensor pipe
 // drains its queue, ~70 cycles per 128x128x16 MMA; a single issuer waiting for
 // P, K and V in series left the pipe idle for about a third of every tile).
-//   QK issuer: QK(g) into score buffer g % 2 for the global tile index g, once
-//              PV(g - 2) (which reads P(g - 2) from that buffer) has completed.
+//   QK issuer: QK(g) into score buffer g % 3 for the global tile index g, once
+//              PV(g - 3) (which reads P(g - 3) from that buffer) has completed.
 //   PV issuer: PV(g) once the softmax has written P(g).
 // Ring positions of an item's K / V tiles (the producer's order): K0 at 0,
 // K1 at 1, then V(j) and K(j + 2) alternate; with e0 the item's first position
@@ -316,17 +300,7 @@ __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
         BW_TRACE_AT(true, 6, g);
         tc_fence_after();
         const uint32_t va = v_lo0 + (e % NS) * (uint32_t)(L::kTile / 16);
-        if constexpr (V == 3) {
-          // part q: O_q += P_q (TMEM columns q K .. q K + K/2 - 1 of the buffer, K = keys
-          // per part) * V rows q K .. q K + K - 1; k-step ks covers V rows 16 ks .. 16 ks + 15
-          constexpr int KSP = Split<D, V>::kKeys / 16;   // k-steps per part
-#pragma unroll
-          for (int ks = 0; ks < kRows / 16; ++ks) {
-            const int q = ks / KSP, kin = ks % KSP;
-            mma_ts_lh(tmem + Split<D, V>::kOCol + q * D, tmem + buf * 128 + q * Split<D, V>::kKeys + kin * 8,
-                      va + (ks * 16 * 128) / 16, HI, IDESC_PV, (kin > 0 || j > 0) ? 1u : 0u);
-          }
-        } else if constexpr (V == 5) {
+        if constexpr (V == 5) {
           // key tile j accumulates into O_{j % 2} (the part that owns it)
           const uint32_t o_col = Split<D, V>::kOCol + (uint32_t)(j & 1) * D;
 #pragma unroll
@@ -358,132 +332,6 @@ __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
 __device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// ----------------------------------------------------------- softmax warps
-// Thread t (0 .. 128 N - 1): row t % 128 of the item's tile (TMEM lane), part
-// t / 128, i.e. keys part K .. part K + K - 1 of every key tile (K = 128 / N).
-template <int D, int POLY>
-__device__ void softmax3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
-  using L = L3<D, 3>;
-  using Split = bw::Split<D, 3>;
-  constexpr int K = Split::kKeys;
-  const int rl = t & 127, part = t >> 7;
-  const uint32_t lane_off = (uint32_t)((rl >> 5) * 32) << 16;
-  constexpr uint32_t NB = Split::NB;
-  const uint32_t o_own = tmem + lane_off + Split::kOCol + part * D;
-  const float c = p.scale_log2;
-  float2* xch = reinterpret_cast<float2*>(smem + L::kX);
-  uint32_t tc = 0, itn = 0;
-
-  for (int idx = blockIdx.x; idx < p.num_items; idx += gridDim.x) {
-    const Item3 it = decode_item3(p, idx);
-    for (int sg = 0; sg < it.nseg; ++sg) {
-    const int n = sg == 0 ? it.n[0] : it.n[1];
-    const int qt = sg == 0 ? it.qt[0] : it.qt[1];
-    const int row = qt * kRows + rl;
-    float m_run = -INFINITY, l_run = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const uint32_t g = tc + j, buf = g % NB;
-      const uint32_t s_tmem = tmem + lane_off + buf * 128 + part * K;
-      if (!wc.wait(&bars.s_full[buf], (g / NB) & 1)) return;
-      BW_TRACE_AT(t == 0, 0, g);
-      BW_TRACE_AT(t == 128, 4, g);
-      tc_fence_after();
-      uint32_t r[K];
-      if constexpr (K == 64) tmem_ld64(s_tmem, r);
-      else tmem_ld32(s_tmem, r);
-      BW_TRACE_AT(t == 0, 1, g);
-      float* s = reinterpret_cast<float*>(r);
-      const int kv0 = j * kRows + part * K;
-      if ((p.causal && kv0 + K - 1 > p.q_offset + qt * kRows) || kv0 + K > p.Skv) {
-        int lim = p.Skv - kv0;
-        if (p.causal) lim = min(lim, p.q_offset + row + 1 - kv0);
-#pragma unroll
-        for (int i = 0; i < K; ++i)
-          if (i >= lim) s[i] = -INFINITY;
-      }
-      float mx;
-      {
-        float a[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) a[u] = fmaxf(s[u], s[8 + u]);
-#pragma unroll
-        for (int i = 16; i < K; i += 16)
-#pragma unroll
-          for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], s[i + u], s[i + 8 + u]);
-        mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
-      }
-      const float m_cand = mx * c;
-      float corr = 1.f;
-      const bool upd = m_cand > m_run + 8.f;
-      if (upd) {
-        corr = ex2_mufu(m_run - m_cand);
-        m_run = m_cand;
-      }
-      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
-      const f2 cc2{c, c}, nm2{-msub, -msub};
-      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f}, acc2{0.f, 0.f}, acc3{0.f, 0.f};
-#pragma unroll
-      for (int k = 0; k < K / 2; ++k) {
-        const f2 x = ffma2(f2{s[2 * k], s[2 * k + 1]}, cc2, nm2);
-        f2 e;
-        if ((k & 7) < POLY) {
-          e = ex2_poly2(x);
-        } else {
-          e.x = ex2_mufu(x.x);
-          e.y = ex2_mufu(x.y);
-        }
-        s[2 * k] = e.x;
-        s[2 * k + 1] = e.y;
-        if ((k & 3) == 0) acc0 = fadd2(acc0, e);
-        else if ((k & 3) == 1) acc1 = fadd2(acc1, e);
-        else if ((k & 3) == 2) acc2 = fadd2(acc2, e);
-        else acc3 = fadd2(acc3, e);
-      }
-      acc0 = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
-      l_run = l_run * corr + (acc0.x + acc0.y);
-      BW_TRACE_AT(t == 0, 2, g);
-      {
-        uint32_t pk[K / 2];
-#pragma unroll
-        for (int k = 0; k < K / 2; ++k) pk[k] = pack_bf16_3(s[2 * k], s[2 * k + 1]);
-        if constexpr (K == 64) tmem_st32(s_tmem, pk);
-        else tmem_st16(s_tmem, pk);
-      }
-      if (j > 0 && __any_sync(0xffffffffu, upd)) {
-        // O_part must hold PV(j - 1) before it is rescaled
-        if (!wc.wait(&bars.pv_done[(g - 1) % NB], ((g - 1) / NB) & 1)) return;
-        tc_fence_after();
-#pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t o[32];
-          tmem_ld32(o_own + c0, o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-          tmem_st32(o_own + c0, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      // one arrival per warp: the warp's TMEM stores are complete (wait::st +
-      // fence above) and ordered before lane 0's arrival by __syncwarp
-      __syncwarp();
-      if ((t & 31) == 0) mbar_arrive(&bars.p_full[buf]);
-      BW_TRACE_AT(t == 0, 3, g);
-      BW_TRACE_AT(t == 128, 5, g);
-      BW_TRACE_AT((t & 31) == 0 && t < 256, 10 + (t >> 5), g);
-    }
-    // hand the row's (m, l) to the epilogue warps (once they have read the
-    // previous segment's) and go on with the next segment
-    if (itn > 0 && !wc.wait(&bars.xch_empty, (itn - 1) & 1)) return;
-    xch[part * kRows + rl] = make_float2(m_run, l_run);
-    __syncwarp();
-    if ((t & 31) == 0) mbar_arrive(&bars.xch_full);
-    tc += n;
-    ++itn;
-    }
-  }
 }
 
 // ------------------------------------------------- softmax warps, kernel 4
@@ -661,8 +509,8 @@ __device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
 // (32x32b shape).  The two warps of one SM sub-partition therefore work on
 // neighbouring key tiles, not on the same one, so one warp's barrier waits and
 // TMEM round trips overlap the other's exponentials.  Each part keeps its own
-// running max and sum; the epilogue merges the two accumulators as in kernel
-// 3.  TMEM: S_0 | S_1 | S_2 | O_0 | O_1 (3 x 128 + 2 x 64 columns); P(g) goes
+// running max and sum; the epilogue merges the two accumulators.  TMEM:
+// S_0 | S_1 | S_2 | O_0 | O_1 (3 x 128 + 2 x 64 columns); P(g) goes
 // over the first 64 columns of its score buffer.  A rescale of O_q at tile j
 // waits for PV(j - 2), the part's previous tile.
 template <int D, int POLY>
@@ -796,7 +644,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) 
 
 // ---------------------------------------------------------- epilogue warps
 // Thread t (0 .. 127): row t of every segment's query tile (TMEM lane t).  Per
-// segment: merge the parts of the row from their (m, l) (m = max_q m_q,
+// segment: merge the parts of the row (kernel 5) from their (m, l) (m = max_q m_q,
 // w_q = 2^(m_q - m) / L, L = sum_q l_q 2^(m_q - m)), read O_0 .. O_{N-1} once
 // PV of the segment's last tile is done, free O for the next segment's first
 // PV, and write O = sum_q w_q O_q through the warp's staging area with TMA
@@ -956,8 +804,7 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
   static_assert(2 * 128 * kSoftRegs + 128 * kEpiRegs + 128 * kAuxRegs <= 65536, "register split");
   if (warp < kSoftWarps) {
     reg_alloc<kSoftRegs>();
-    if constexpr (V == 3) softmax3<D, POLY>(p, smem, bars, wc, tmem, tid);
-    else if constexpr (V == 5) softmax5<D, POLY>(p, smem, bars, wc, tmem, tid);
+    if constexpr (V == 5) softmax5<D, POLY>(p, smem, bars, wc, tmem, tid);
     else softmax4<D, POLY>(p, smem, bars, wc, tmem, tid);
   } else if (warp < kEpilogue + 4) {
     reg_dealloc<kEpiRegs>();   // 128 keeps the launch count; states this role's bound to the register allocator
@@ -1003,13 +850,6 @@ cudaError_t launch3_poly(const FmhaParams& p, const FmhaMaps& maps, int poly, in
 }
 
 }  // namespace
-
-cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
-                             cudaStream_t stream) {
-  if (p.D == 128) return launch3_poly<128, 3>(p, maps, exp_poly, num_sms, stream);
-  if (p.D == 64) return launch3_poly<64, 3>(p, maps, exp_poly, num_sms, stream);
-  return cudaErrorInvalidValue;
-}
 
 cudaError_t launch_fmha_fwd5(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream) {

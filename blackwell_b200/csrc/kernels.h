@@ -17,9 +17,7 @@ struct FmhaParams {
   int causal;                    // 1: key j visible to query i iff j <= i
   float scale_log2;              // softmax scale * log2(e)
   int n_qtiles, n_kvtiles;       // ceil(Sq / 128), ceil(Skv / 128)
-  int pair_heads;                // 1: a CTA work item = two heads of one KV group,
-                                 //    same 128-row query tile; 0: two query tiles of one head
-  int num_items;
+  int num_items;                 // work items (one query tile, or a causal pair of them)
   int* err;                      // device error word
   uint64_t timeout_ns;           // bound for every device-side wait
   int debug_flags;               // bit 0: producer withholds its first K load (timeout test)
@@ -32,14 +30,8 @@ struct FmhaParams {
 struct FmhaMaps {
   CUtensorMap q, k, v;           // 4-D (D, S, H, B) bf16, box (64, rows, 1, 1), SWIZZLE_128B;
                                  // rows = 128
-  CUtensorMap o;                 // launch_fmha_fwd3 only: 4-D (D, Sq, Hq, B) bf16 output, box (64, 32, 1, 1),
-                                 // SWIZZLE_128B
+  CUtensorMap o;                 // 4-D (D, Sq, Hq, B) bf16 output, box (64, 32, 1, 1), SWIZZLE_128B
 };
-
-// exp_poly: of every 8 pairs of exponentials, how many run as the FMA-pipe
-// polynomial instead of MUFU ex2 (0, 2, 3 or 4).
-cudaError_t launch_fmha_fwd(const FmhaParams& p, const FmhaMaps& maps, bool p_in_tmem, int exp_poly, int num_sms,
-                            cudaStream_t stream);
 
 // fp32 MHA at fp32 accuracy (3xTF32 split, D = 64): split passes and the
 // attention kernel (fmha_f32x3.cu).  The split arrays: Q and K hi / lo as
@@ -66,12 +58,11 @@ cudaError_t launch_f32x3_split_vt(const float* x, int64_t sb, int64_t sh, int64_
                                   int H, int S, int S32, cudaStream_t stream);
 cudaError_t launch_fmha_f32x3(const F32x3Params& p, const F32x3Maps& maps, cudaStream_t stream);
 
-// One query tile per work item, double-buffered scores (one softmax warpgroup).
-cudaError_t launch_fmha_fwd3(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
-                             cudaStream_t stream);
-// Kernel 4: kernel 3's roles with one O accumulator and three score buffers
-// (rows read through the 16-lane TMEM shapes, four threads per row sharing
-// the running max).
+// Prefill kernels (fmha_fwd3.cu), one query tile per work item.  exp_poly: of
+// every 8 pairs of exponentials, how many run as the FMA-pipe polynomial
+// instead of MUFU ex2 (0, 2, 3 or 4).
+// Kernel 4: three score buffers and one O accumulator (rows read through the
+// 16-lane TMEM shapes, four threads per row sharing the running max).
 cudaError_t launch_fmha_fwd4(const FmhaParams& p, const FmhaMaps& maps, int exp_poly, int num_sms,
                              cudaStream_t stream);
 // Kernel 5 (D = 64): three score buffers, two O accumulators; the two softmax

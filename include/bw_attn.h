@@ -240,8 +240,6 @@ BW_API int bw_stream_status(void* stream);
 
 /* Library options (process-wide).  Keys:
  *   BW_OPT_TIMEOUT_NS      bound on every device-side wait (default 2e9)
- *   BW_OPT_P_IN_TMEM       1 (default): P feeds the PV MMA from tensor memory;
- *                          0: through a swizzled shared-memory tile
  *   BW_OPT_DEBUG_FLAGS     test hook; bit 0 makes the prefill producer withhold
  *                          its first K tile so that the consumers' bounded waits
  *                          expire and the call reports BW_ERR_TIMEOUT
@@ -253,20 +251,19 @@ BW_API int bw_stream_status(void* stream);
  *   BW_OPT_PREFILL_KERNEL  0 (default): kernel 5 at D = 64, kernel 4 at
  *                          D = 128 (the fastest at every measured shape on
  *                          B200);
- *                          1: two 128-row query blocks per CTA sharing each K/V
- *                          tile, one score buffer per block;
- *                          3: one query block per CTA, two score buffers, each
- *                          row's keys split over two threads with independent
- *                          softmax states merged by separate epilogue warps,
- *                          separate QK^T and PV issuing threads;
- *                          4: as 3 with three score buffers and one O
- *                          accumulator (four threads per row share the
- *                          running max), so QK^T never waits for PV;
+ *                          4: one query tile per CTA, three score buffers and
+ *                          one O accumulator (four threads per row share the
+ *                          running max), separate QK^T and PV issuing threads
+ *                          and an epilogue warpgroup, so QK^T never waits for
+ *                          the PV of the previous tile;
  *                          5 (D = 64; at D = 128 it selects 4): three score
  *                          buffers and two O accumulators, the two softmax
  *                          warpgroups taking alternate key tiles (one row per
  *                          thread), merged by the epilogue warps.
- *                          BW_OPT_P_IN_TMEM applies to kernel 1 only. */
+ *                          Other values return BW_ERR_SHAPE (kernels 1-3 were
+ *                          removed as slower at every measured shape).
+ *   BW_OPT_P_IN_TMEM       retired with kernel 1; setting it returns
+ *                          BW_ERR_SHAPE. */
 enum {
   BW_OPT_TIMEOUT_NS = 1,
   BW_OPT_P_IN_TMEM = 2,

@@ -139,8 +139,10 @@ def test_prefill_kernel_option_values():
     lib = _ffi.lib()
     old = lib.bw_get_option(_ffi.BW_OPT_PREFILL_KERNEL)
     assert old == 0                                   # default kernel
-    for v in (0, 1, 3, 4, 5):
+    for v in (0, 4, 5):
         assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == 0
-    for v in (-1, 2, 6):
+    for v in (-1, 1, 2, 3, 6):                        # kernels 1-3 were removed
         assert lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, v) == _ffi.BW_ERR_SHAPE
     lib.bw_set_option(_ffi.BW_OPT_PREFILL_KERNEL, old)
+    # the P-in-TMEM switch went with kernel 1
+    assert lib.bw_set_option(_ffi.BW_OPT_P_IN_TMEM, 1) == _ffi.BW_ERR_SHAPE

@@ -12,8 +12,8 @@ from tests._util import seeded_bf16
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kernel,D", [(0, 64), (0, 128), (1, 128), (1, 64), (4, 128), (4, 64), (5, 64)],
-                         ids=["auto_d64", "auto_d128", "k1_d128", "k1_d64", "k4_d128", "k4_d64", "k5_d64"])
+@pytest.mark.parametrize("kernel,D", [(0, 64), (0, 128), (4, 128), (4, 64), (5, 64)],
+                         ids=["auto_d64", "auto_d128", "k4_d128", "k4_d64", "k5_d64"])
 def test_withheld_tile_reports_timeout_and_recovers(kernel, D):
     """Each prefill kernel at both head dimensions: the withheld K tile makes
     every role's bounded wait expire."""
