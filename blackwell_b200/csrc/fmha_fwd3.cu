@@ -66,10 +66,10 @@ struct Split {
   // QK issuer (+ one idle warp): four warpgroups for the register split
   static constexpr int kThreads = 512;
   static_assert(N == 2, "warpgroup roles assume two softmax warpgroups");
-  static_assert(kOCol + NACC * D <= 512, "TMEM: score buffers, P buffers and accumulators");
+  static_assert(kOCol + NACC * D <= 512, "TMEM: score buffers and accumulators");
 };
 
-template <int D, int V = 4>
+template <int D>
 struct L3 {
   static constexpr int kTile = kRows * D * 2;   // one 128-row bf16 tile
   static constexpr int kSub = kRows * 128;      // one 128-byte swizzle panel
@@ -138,7 +138,7 @@ __device__ __forceinline__ Item3 decode_item3(const FmhaParams& p, int idx) {
 // thread consumes them: K0, K1, then V(j), K(j + 2) for j = 0 .. n - 1.
 template <int D, int V>
 __device__ void producer3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc) {
-  using L = L3<D, V>;
+  using L = L3<D>;
   constexpr int NS = L::NS;
   uint32_t ld = 0, qn = 0;
   uint32_t armed = 0;
@@ -228,7 +228,7 @@ __device__ __forceinline__ uint32_t pos_v(int j, int n) {
 
 template <int D, int V>
 __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
-  using L = L3<D, V>;
+  using L = L3<D>;
   constexpr int NS = L::NS;
   constexpr int SUB = L::kSub;
   constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 128, false);
@@ -277,7 +277,7 @@ __device__ void qk_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, cons
 
 template <int D, int V>
 __device__ void pv_issuer3(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem) {
-  using L = L3<D, V>;
+  using L = L3<D>;
   constexpr int NS = L::NS;
   constexpr int SUB = L::kSub;
   constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, D, true);
@@ -345,7 +345,7 @@ __device__ __forceinline__ uint32_t pack_bf16_3(float lo, float hi) {
 // MMA reads it (key k at column k / 2).
 template <int D, int POLY>
 __device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
-  using L = L3<D, 4>;
+  using L = L3<D>;
   using Split = bw::Split<D, 4>;
   constexpr uint32_t NB = Split::NB;
   const int w = t >> 5, ln = t & 31;
@@ -515,7 +515,7 @@ __device__ void softmax4(const FmhaParams& p, uint8_t* smem, Bars3& bars, const 
 // waits for PV(j - 2), the part's previous tile.
 template <int D, int POLY>
 __device__ void softmax5(const FmhaParams& p, uint8_t* smem, Bars3& bars, const WaitCtl& wc, uint32_t tmem, int t) {
-  using L = L3<D, 5>;
+  using L = L3<D>;
   using Split = bw::Split<D, 5>;
   constexpr uint32_t NB = Split::NB;
   const int rl = t & 127, part = t >> 7;
@@ -655,7 +655,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) 
 template <int D, int V>
 __device__ void epilogue3(const FmhaParams& p, const FmhaMaps& maps, uint8_t* smem, Bars3& bars, const WaitCtl& wc,
                           uint32_t tmem, int t) {
-  using L = L3<D, V>;
+  using L = L3<D>;
   constexpr int N = Split<D, V>::NACC;
   const int ln = t & 31, wq = t >> 5;
   const uint32_t o0 = tmem + ((uint32_t)(wq * 32) << 16) + Split<D, V>::kOCol;
@@ -742,7 +742,7 @@ template <int D, int POLY, int V>
 __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, const __grid_constant__ FmhaMaps maps) {
   using Split = bw::Split<D, V>;
   static_assert(Split::kThreads == 512, "launch bounds");
-  using L = L3<D, V>;
+  using L = L3<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   if (pad > (uint32_t)kAlignSlack) {
@@ -829,7 +829,7 @@ __global__ void __launch_bounds__(512, 1) fmha_fwd3_kernel(const FmhaParams p, c
 
 template <int D, int POLY, int V>
 cudaError_t launch3(const FmhaParams& p, const FmhaMaps& maps, int num_sms, cudaStream_t stream) {
-  constexpr int bytes = L3<D, V>::kBytes + kAlignSlack;
+  constexpr int bytes = L3<D>::kBytes + kAlignSlack;
   auto kern = fmha_fwd3_kernel<D, POLY, V>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
