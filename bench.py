@@ -599,7 +599,7 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not (args.no_secondary or args.profile):
         del hq_, hk_, hv_, ws
         torch.cuda.empty_cache()
-        sec_steps = max(5, min(args.steps // 10, 50))
+        sec_steps = max(20, min(args.steps // 10, 50))
         secondary["C3_mha_D64"] = bench_prefill((8, 16, 16, 2048, 64), False, "bhsd", flush, sec_steps, 3)
         secondary["C3_mha_D128"] = bench_prefill((8, 16, 16, 2048, 128), False, "bhsd", flush, sec_steps, 3)
         ref_shape = bench_prefill((8, 12, 4, 4096, 64), True, "bhsd", flush, sec_steps, 3)
