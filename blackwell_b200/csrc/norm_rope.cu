@@ -17,7 +17,8 @@
 // elements sits D/2 elements away, in lane l ^ (LPR/2) (one shuffle); GPT-J
 // pairs are inside a lane.  The row's norm is a shuffle reduction over its LPR
 // lanes.  cos/sin are read with 16-byte loads (the cache is 16-byte aligned and
-// a row is D*4 bytes).  Grid-stride over row groups, grid sized to the SM count.
+// a row is D*4 bytes).  Grid-stride over row groups, grid sized to the SM count;
+// rows are walked in memory order of the input layout (BHSD or BSHD).
 #include <cuda_bf16.h>
 
 #include "kernels.h"
@@ -49,6 +50,7 @@ __global__ void __launch_bounds__(256, kMinBlocks) norm_rope_kernel(const NormRo
   const int ci = 8 * sub;              // first cos / sin index this lane uses (8 of them)
   const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
   const uint32_t rows = (uint32_t)p.B * p.H * p.S;   // < 2^31, checked by the caller
+  const bool s_fast = p.in_ss <= p.in_sh;
 
   for (uint32_t base = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW; base < rows;
        base += warps_total * RPW) {
@@ -56,22 +58,40 @@ __global__ void __launch_bounds__(256, kMinBlocks) norm_rope_kernel(const NormRo
     int64_t out_off[kGroups];
     int pos[kGroups];
     uint32_t rs_idx[kGroups];  // [B, H, S] index of the row (rstd output)
-    // Rows are enumerated (b, s, h) with h fastest, so the rows in flight share
-    // few positions and their cos/sin reads hit L1.  (b, s, h) of this lane's
-    // first row by division, the later ones by stepping h forward RPI at a time.
+    // Rows are enumerated with the dimension of smaller input stride fastest
+    // ((b, h, s) for BHSD, (b, s, h) for BSHD), so the rows in flight are
+    // neighbours in memory (the other order cost 8 % at the BHSD C2 shape).
+    // The first row of this lane by division, the later ones by stepping the
+    // fast index forward RPI at a time.
     uint32_t r = base + lane / LPR;
     if (r >= rows) r = rows - 1;
-    uint32_t bs = r / (uint32_t)p.H;
-    int h = (int)(r - bs * (uint32_t)p.H);
-    int b = (int)(bs / (uint32_t)p.S);
-    int s = (int)(bs - (uint32_t)b * p.S);
+    int b, h, s;
+    if (s_fast) {
+      const uint32_t bh = r / (uint32_t)p.S;
+      s = (int)(r - bh * (uint32_t)p.S);
+      b = (int)(bh / (uint32_t)p.H);
+      h = (int)(bh - (uint32_t)b * p.H);
+    } else {
+      const uint32_t bs = r / (uint32_t)p.H;
+      h = (int)(r - bs * (uint32_t)p.H);
+      b = (int)(bs / (uint32_t)p.S);
+      s = (int)(bs - (uint32_t)b * p.S);
+    }
 #pragma unroll
     for (int u = 0; u < kGroups; ++u) {
       if (u > 0 && base + u * RPI + lane / LPR < rows) {
-        h += RPI;
-        while (h >= p.H) {
-          h -= p.H;
-          if (++s == p.S) { s = 0; ++b; }
+        if (s_fast) {
+          s += RPI;
+          while (s >= p.S) {
+            s -= p.S;
+            if (++h == p.H) { h = 0; ++b; }
+          }
+        } else {
+          h += RPI;
+          while (h >= p.H) {
+            h -= p.H;
+            if (++s == p.S) { s = 0; ++b; }
+          }
         }
       }
       const __nv_bfloat16* src =
